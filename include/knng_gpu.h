@@ -1,0 +1,119 @@
+/*
+ * knng_gpu.h -- C ABI of the B200 brute-force KNN-graph builder
+ * (libknng_gpu.so). Plain pointers and sizes only; no C++ or torch types.
+ *
+ * The reference has no FFI: its boundary is the C++ template
+ *   template <Distance D>
+ *   Knng knng::cpu::brute_force_knn(const Dataset& ds, std::size_t k, D d = D{});
+ * (include/knng/cpu/brute_force.hpp:336-337, instantiated for L2Squared and
+ * NegativeInnerProduct at src/cpu/brute_force.cpp:39-43). These entry points
+ * are what a binding of that template to a GPU library needs; the header-only
+ * C++ drop-in include/knng/gpu/brute_force.hpp wraps them back into the
+ * reference's signature.
+ *
+ * Output layout (every entry point): row q of the graph is
+ *   ids[q*k .. q*k+k), dists[q*k .. q*k+k)
+ * sorted ascending by (distance, id), self excluded by index: the layout of
+ * knng::Knng (include/knng/core/graph.hpp:35-84).
+ *
+ * Errors: every entry point returns a knng_gpu_status and never aborts; the
+ * message of the last failure on the calling thread is knng_gpu_last_error().
+ * Argument errors use the reference's wording (brute_force.hpp:339-352).
+ */
+#ifndef KNNG_GPU_H
+#define KNNG_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    KNNG_GPU_OK = 0,
+    KNNG_GPU_INVALID_ARGUMENT = 1, /* maps to std::invalid_argument */
+    KNNG_GPU_CUDA_ERROR = 2,       /* a CUDA runtime/driver call failed */
+    KNNG_GPU_TIMEOUT = 3,          /* a bounded device-side wait gave up */
+    KNNG_GPU_NOT_SUPPORTED = 4,    /* e.g. k above KNNG_GPU_MAX_K */
+    KNNG_GPU_OUT_OF_MEMORY = 5,
+    KNNG_GPU_WORKSPACE_TOO_SMALL = 6
+} knng_gpu_status;
+
+/* Metric ids equal the .knng file header's metric_id
+ * (tools/build_knng.cpp:183-188): 0 = L2Squared, 1 = NegativeInnerProduct. */
+typedef enum { KNNG_METRIC_L2_SQUARED = 0, KNNG_METRIC_NEGATIVE_INNER_PRODUCT = 1 } knng_metric;
+
+/* Which kernel family produced the result. */
+typedef enum { KNNG_PATH_U8_TENSOR = 0, KNNG_PATH_F32_EXACT = 1 } knng_path;
+
+#define KNNG_GPU_MAX_K 1024u
+
+typedef struct {
+    int path;                 /* knng_path */
+    uint64_t fallback_rows;   /* u8-path rows recomputed by the exact kernel */
+    float pack_ms;            /* integer check + u8 pack + row norms */
+    float knn_ms;             /* fused KNN kernel (device time, CUDA events) */
+    float fallback_ms;        /* exact kernel on fallback rows */
+    float total_ms;           /* whole call, device time */
+    uint32_t kernel_launches; /* kernels this call launched */
+} knng_gpu_stats;
+
+/* Message of the last failure on this thread ("" if none). */
+const char* knng_gpu_last_error(void);
+
+/* Number of CUDA devices visible (0 if none / no driver). */
+int knng_gpu_device_count(void);
+
+/* ---- one-shot host API (the drop-in) ------------------------------------
+ * Replaces knng::cpu::brute_force_knn<L2Squared|NegativeInnerProduct>
+ * (include/knng/cpu/brute_force.hpp:336-376). `data` is the row-major
+ * n x d fp32 payload of a knng::Dataset (dataset.hpp:76-152, data_ptr()),
+ * `ids`/`dists` are caller-allocated n*k arrays (Knng::neighbors/distances).
+ * Runs on the current CUDA device; allocates and frees its device memory
+ * inside the call. `stats` may be NULL. */
+knng_gpu_status knng_gpu_brute_force(const float* data, uint64_t n, uint64_t d, uint64_t k, int metric,
+                                     uint32_t* ids, float* dists, knng_gpu_stats* stats);
+
+/* ---- device-resident API (inputs already in HBM) ------------------------
+ * All pointers are device pointers; `stream` is a cudaStream_t (NULL = the
+ * legacy default stream). Nothing is allocated: the caller passes a
+ * workspace of at least knng_gpu_workspace_bytes(n, d) bytes, 256-byte
+ * aligned. Same semantics and output layout as knng_gpu_brute_force; the
+ * call synchronises `stream` once (to read which path applies). */
+uint64_t knng_gpu_workspace_bytes(uint64_t n, uint64_t d);
+knng_gpu_status knng_gpu_brute_force_device(const float* d_data, uint64_t n, uint64_t d, uint64_t k, int metric,
+                                            uint32_t* d_ids, float* d_dists, void* d_workspace,
+                                            uint64_t workspace_bytes, void* stream, knng_gpu_stats* stats);
+
+/* ---- building blocks for sharded (multi-GPU) builds ---------------------
+ * The distributed driver (one process per GPU) packs its slice of rows,
+ * exchanges packed rows with NCCL, and runs the fused kernel on its query
+ * shard against the full base, mirroring the reference's query sharding
+ * (include/knng/dist/sharded_dataset.hpp:145-155, src/dist/brute_force_mpi.cpp:36-142).
+ *
+ * knng_gpu_padded_dim: row pitch in bytes of the packed u8 layout (d rounded up to 128).
+ * knng_gpu_pack_u8: rows x d fp32 -> rows x pitch u8 + int32 |x|^2 per row;
+ *   atomically ORs 1 into *d_nonint if any value is not an integer in [0,255]
+ *   (then the packed output is meaningless and the fp32 path must be used).
+ * knng_gpu_knn_u8: queries are packed rows [q_begin, q_begin+q_count) of the
+ *   base; results for query row i go to row i of d_ids/d_dists (q_count x k).
+ *   d_scratch: >= knng_gpu_knn_scratch_bytes(q_count) bytes.
+ * knng_gpu_knn_f32: exact fp32 kernel on raw rows (any values). */
+uint64_t knng_gpu_padded_dim(uint64_t d);
+knng_gpu_status knng_gpu_pack_u8(const float* d_x, uint64_t rows, uint64_t d, uint8_t* d_packed,
+                                 int32_t* d_norms, int32_t* d_nonint, void* stream);
+uint64_t knng_gpu_knn_scratch_bytes(uint64_t q_count);
+knng_gpu_status knng_gpu_knn_u8(const uint8_t* d_packed, const int32_t* d_norms, uint64_t n, uint64_t d,
+                                uint64_t q_begin, uint64_t q_count, uint64_t k, int metric, uint32_t* d_ids,
+                                float* d_dists, void* d_scratch, uint64_t scratch_bytes, void* stream,
+                                knng_gpu_stats* stats);
+knng_gpu_status knng_gpu_knn_f32(const float* d_x, uint64_t n, uint64_t d, uint64_t q_begin, uint64_t q_count,
+                                 uint64_t k, int metric, uint32_t* d_ids, float* d_dists, void* stream,
+                                 knng_gpu_stats* stats);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KNNG_GPU_H */

@@ -1,0 +1,23 @@
+"""knng_gpu_b200 -- exact brute-force KNN-graph construction on NVIDIA B200.
+
+A drop-in GPU counterpart of ``knng::cpu::brute_force_knn`` from the
+reference project (include/knng/cpu/brute_force.hpp:336-376): hand-written
+sm_100a kernels behind the C ABI of ``include/knng_gpu.h``.
+"""
+from .api import (  # noqa: F401
+    Dataset,
+    InvalidArgument,
+    Knng,
+    KnngGpuError,
+    L2Squared,
+    NegativeInnerProduct,
+    brute_force_knn,
+    brute_force_knn_device,
+    device_count,
+    knn_f32,
+    knn_scratch_bytes,
+    knn_u8,
+    pack_u8,
+    padded_dim,
+    workspace_bytes,
+)

@@ -1,0 +1,231 @@
+"""Host-side mirror of the reference's brute-force API, backed by the C ABI.
+
+The reference's boundary (include/knng/cpu/brute_force.hpp:336-376) is::
+
+    template <Distance D>
+    Knng knng::cpu::brute_force_knn(const Dataset& ds, std::size_t k, D d = D{});
+
+This module keeps the same names, argument meaning and error behaviour:
+``Dataset`` (include/knng/core/dataset.hpp:76-152), ``Knng``
+(include/knng/core/graph.hpp:35-84), the two metrics of
+include/knng/core/distance.hpp:86-116, and ``brute_force_knn`` raising
+:class:`InvalidArgument` (a ``ValueError``, the analogue of
+``std::invalid_argument``) for n == 0, k == 0 and k > n - 1 with the
+reference's messages. Everything runs on the GPU through ``libknng_gpu.so``;
+there is no CPU path here.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from ._native import KnngGpuStats, gpu_lib
+
+STATUS_NAMES = {
+    0: "OK",
+    1: "INVALID_ARGUMENT",
+    2: "CUDA_ERROR",
+    3: "TIMEOUT",
+    4: "NOT_SUPPORTED",
+    5: "OUT_OF_MEMORY",
+    6: "WORKSPACE_TOO_SMALL",
+}
+
+
+class KnngGpuError(RuntimeError):
+    """A non-argument failure of the GPU library (CUDA error, timeout, ...)."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+class InvalidArgument(ValueError):
+    """Raised where the reference throws std::invalid_argument."""
+
+
+class L2Squared:
+    """knng::L2Squared (distance.hpp:86-95); metric id 0."""
+
+    metric_id = 0
+
+
+class NegativeInnerProduct:
+    """knng::NegativeInnerProduct (distance.hpp:105-116); metric id 1."""
+
+    metric_id = 1
+
+
+@dataclass
+class Dataset:
+    """Row-major n x d fp32 feature matrix (knng::Dataset)."""
+
+    n: int = 0
+    d: int = 0
+    data: np.ndarray = field(default_factory=lambda: np.zeros(0, np.float32))
+
+    @staticmethod
+    def from_array(x: np.ndarray) -> "Dataset":
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim != 2:
+            raise InvalidArgument("Dataset.from_array: expected a 2-D array")
+        return Dataset(x.shape[0], x.shape[1], x.reshape(-1))
+
+    def row(self, i: int) -> np.ndarray:
+        return self.data[i * self.d:(i + 1) * self.d]
+
+    def data_ptr(self) -> int:
+        return self.data.ctypes.data
+
+    def is_contiguous(self) -> bool:
+        return self.data.size == self.n * self.d
+
+
+@dataclass
+class Knng:
+    """Flat (n, k) adjacency: knng::Knng (graph.hpp:35-84)."""
+
+    n: int
+    k: int
+    neighbors: np.ndarray  # uint32[n*k]
+    distances: np.ndarray  # float32[n*k]
+    stats: dict | None = None
+
+    def neighbors_of(self, i: int) -> np.ndarray:
+        return self.neighbors[i * self.k:(i + 1) * self.k]
+
+    def distances_of(self, i: int) -> np.ndarray:
+        return self.distances[i * self.k:(i + 1) * self.k]
+
+
+def _metric_id(distance) -> int:
+    if isinstance(distance, (int, np.integer)):
+        return int(distance)
+    if isinstance(distance, str):
+        return {"l2": 0, "negip": 1}[distance]
+    mid = getattr(distance, "metric_id", None)
+    if mid is None:
+        raise TypeError("brute_force_knn: distance must be L2Squared or NegativeInnerProduct")
+    return mid
+
+
+def _last_error() -> str:
+    msg = gpu_lib().knng_gpu_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(status: int) -> None:
+    """Raise the Python analogue of the C status (no-op for OK)."""
+    if status == 0:
+        return
+    msg = _last_error()
+    if status == 1:
+        raise InvalidArgument(msg)
+    raise KnngGpuError(status, msg)
+
+
+def brute_force_knn(ds: Dataset | np.ndarray, k: int, distance=L2Squared()) -> Knng:
+    """Exact all-points KNN graph on the GPU; drop-in for knng::cpu::brute_force_knn.
+
+    Rows are sorted ascending by (distance, id); self is excluded by index.
+    """
+    if isinstance(ds, np.ndarray):
+        ds = Dataset.from_array(ds)
+    if k < 0:
+        raise InvalidArgument("knng::gpu::brute_force_knn: k must be > 0")
+    data = np.ascontiguousarray(ds.data, dtype=np.float32)
+    n, d = int(ds.n), int(ds.d)
+    ids = np.empty(max(n * k, 1), dtype=np.uint32)
+    dists = np.empty(max(n * k, 1), dtype=np.float32)
+    stats = KnngGpuStats()
+    st = gpu_lib().knng_gpu_brute_force(
+        data.ctypes.data if data.size else None, n, d, k, _metric_id(distance),
+        ids.ctypes.data, dists.ctypes.data, ctypes.byref(stats))
+    check(st)
+    return Knng(n, k, ids[: n * k], dists[: n * k], stats.as_dict())
+
+
+# ---------------------------------------------------------------- device API
+def _ptr(t) -> int | None:
+    return None if t is None else int(t.data_ptr())
+
+
+def _stream_handle(stream) -> int | None:
+    if stream is None:
+        import torch
+
+        stream = torch.cuda.current_stream()
+    return int(stream.cuda_stream)
+
+
+def workspace_bytes(n: int, d: int) -> int:
+    return int(gpu_lib().knng_gpu_workspace_bytes(n, d))
+
+
+def brute_force_knn_device(x, k: int, distance=L2Squared(), out_ids=None, out_dists=None, workspace=None,
+                           stream=None):
+    """Device-resident build: ``x`` is a CUDA float32 (n, d) torch tensor.
+
+    Returns ``(ids, dists, stats)`` as CUDA tensors of shape (n, k) and a
+    dict of device timings. ``workspace`` (uint8 CUDA tensor of at least
+    :func:`workspace_bytes` bytes) is allocated here when not given.
+    """
+    import torch
+
+    if x.dim() != 2 or x.dtype != torch.float32 or not x.is_cuda or not x.is_contiguous():
+        raise InvalidArgument("brute_force_knn_device: x must be a contiguous CUDA float32 (n, d) tensor")
+    n, d = x.shape
+    dev = x.device
+    if out_ids is None:
+        out_ids = torch.empty((n, max(k, 0)), dtype=torch.int32, device=dev)
+    if out_dists is None:
+        out_dists = torch.empty((n, max(k, 0)), dtype=torch.float32, device=dev)
+    wsb = workspace_bytes(n, d)
+    if workspace is None:
+        workspace = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    stats = KnngGpuStats()
+    st = gpu_lib().knng_gpu_brute_force_device(
+        _ptr(x), n, d, k, _metric_id(distance), _ptr(out_ids), _ptr(out_dists), _ptr(workspace),
+        workspace.numel(), _stream_handle(stream), ctypes.byref(stats))
+    check(st)
+    return out_ids, out_dists, stats.as_dict()
+
+
+def padded_dim(d: int) -> int:
+    return int(gpu_lib().knng_gpu_padded_dim(d))
+
+
+def pack_u8(x, packed, norms, nonint_flag, stream=None) -> None:
+    """u8 pack + integer check + row norms of a CUDA float32 (rows, d) tensor."""
+    rows, d = x.shape
+    check(gpu_lib().knng_gpu_pack_u8(_ptr(x), rows, d, _ptr(packed), _ptr(norms), _ptr(nonint_flag),
+                                     _stream_handle(stream)))
+
+
+def knn_scratch_bytes(q_count: int) -> int:
+    return int(gpu_lib().knng_gpu_knn_scratch_bytes(q_count))
+
+
+def knn_u8(packed, norms, n: int, d: int, q_begin: int, q_count: int, k: int, distance, out_ids, out_dists,
+           scratch, stream=None) -> dict:
+    """Fused tensor-core KNN of packed query rows [q_begin, q_begin+q_count) against all n rows."""
+    stats = KnngGpuStats()
+    check(gpu_lib().knng_gpu_knn_u8(_ptr(packed), _ptr(norms), n, d, q_begin, q_count, k, _metric_id(distance),
+                                    _ptr(out_ids), _ptr(out_dists), _ptr(scratch), scratch.numel(),
+                                    _stream_handle(stream), ctypes.byref(stats)))
+    return stats.as_dict()
+
+
+def knn_f32(x, n: int, d: int, q_begin: int, q_count: int, k: int, distance, out_ids, out_dists,
+            stream=None) -> dict:
+    """Exact fp32 KNN of rows [q_begin, q_begin+q_count) of x against all n rows."""
+    stats = KnngGpuStats()
+    check(gpu_lib().knng_gpu_knn_f32(_ptr(x), n, d, q_begin, q_count, k, _metric_id(distance), _ptr(out_ids),
+                                     _ptr(out_dists), _stream_handle(stream), ctypes.byref(stats)))
+    return stats.as_dict()
+
+
+def device_count() -> int:
+    return int(gpu_lib().knng_gpu_device_count())

@@ -1,0 +1,122 @@
+/*
+ * synthetic.c -- seeded synthetic datasets for the benchmark configurations
+ * (host C, libknng_synth.so). Every dataset is drawn row-major from one
+ * knng::random::XorShift64 stream (include/knng/random.hpp:48-144): the
+ * (13, 7, 17) xorshift, next_float01 = top 24 bits / 2^24, next_below =
+ * Lemire multiply-high, as in the reference's bench generator
+ * (benchmarks/bench_brute_force.cpp:57-68).
+ *
+ * Recipes (kind):
+ *   0  uniform integers:   x = (float) next_below(256)
+ *   1  Gaussian mixture:   `components` centres, each coordinate
+ *                          2*next_float01()-1 (all centres first); then per
+ *                          point c = next_below(components) and per
+ *                          coordinate x = centre + sigma * z, z standard
+ *                          normal by Box-Muller on two next_float01() draws:
+ *                          z = sqrt(-2 ln(1-u1)) * cos(2 pi u2) in double,
+ *                          rounded to float once.
+ *   2  unit rows:          x = next_float01(), then every row divided by
+ *                          sqrtf of its sequential fp32 sum of squares
+ *   3  sparse integers:    next_float01() < p_zero ? 0 : 1 + next_below(255)
+ *   4  uniform [-1, 1):    2*next_float01()-1 (the reference bench's data)
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+
+static uint64_t xs_next(uint64_t *s)
+{
+    uint64_t x = *s;
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    *s = x;
+    return x;
+}
+
+static float xs_float01(uint64_t *s)
+{
+    const uint64_t bits = (xs_next(s) >> 40) & ((1ull << 24) - 1);
+    return (float)bits * (1.0f / (float)(1u << 24));
+}
+
+static uint64_t xs_below(uint64_t *s, uint64_t bound)
+{
+    if (bound <= 1) return 0;
+    const unsigned __int128 p = (unsigned __int128)xs_next(s) * bound;
+    return (uint64_t)(p >> 64);
+}
+
+/* Returns 0 on success, -1 for an unknown kind or a zero seed. `scratch`
+ * must hold components*d floats for kind 1 (may be NULL otherwise). */
+int knng_synth_generate(int kind, uint64_t seed, uint64_t n, uint64_t d, float *out, uint64_t components,
+                        float sigma, float p_zero, float *scratch)
+{
+    if (seed == 0) return -1;
+    uint64_t s = seed;
+    switch (kind) {
+    case 0:
+        for (uint64_t i = 0; i < n * d; ++i) out[i] = (float)xs_below(&s, 256);
+        return 0;
+    case 1: {
+        if (!scratch || components == 0) return -1;
+        for (uint64_t i = 0; i < components * d; ++i) scratch[i] = 2.0f * xs_float01(&s) - 1.0f;
+        const double two_pi = 6.283185307179586476925286766559;
+        for (uint64_t r = 0; r < n; ++r) {
+            const float *c = scratch + xs_below(&s, components) * d;
+            for (uint64_t j = 0; j < d; ++j) {
+                const double u1 = (double)xs_float01(&s);
+                const double u2 = (double)xs_float01(&s);
+                const float z = (float)(sqrt(-2.0 * log(1.0 - u1)) * cos(two_pi * u2));
+                out[r * d + j] = c[j] + sigma * z;
+            }
+        }
+        return 0;
+    }
+    case 2:
+        for (uint64_t r = 0; r < n; ++r) {
+            float *row = out + r * d;
+            float acc = 0.0f;
+            for (uint64_t j = 0; j < d; ++j) {
+                row[j] = xs_float01(&s);
+                const float sq = row[j] * row[j];
+                acc = acc + sq;
+            }
+            const float norm = sqrtf(acc);
+            if (norm > 0.0f)
+                for (uint64_t j = 0; j < d; ++j) row[j] = row[j] / norm;
+        }
+        return 0;
+    case 3:
+        for (uint64_t i = 0; i < n * d; ++i) out[i] = xs_float01(&s) < p_zero ? 0.0f : (float)(1 + xs_below(&s, 255));
+        return 0;
+    case 4:
+        for (uint64_t i = 0; i < n * d; ++i) out[i] = 2.0f * xs_float01(&s) - 1.0f;
+        return 0;
+    default:
+        return -1;
+    }
+}
+
+/* Sorted, distinct query ids for the subset harness: ids drawn with
+ * next_below(n), repeats rejected, until `count` distinct ids are held;
+ * returned in ascending order. */
+int knng_synth_sample_ids(uint64_t seed, uint64_t n, uint64_t count, uint64_t *out)
+{
+    if (seed == 0 || count > n) return -1;
+    const uint64_t words = (n + 63) / 64;
+    uint64_t *bits = (uint64_t *)calloc(words, sizeof(uint64_t));
+    if (!bits) return -1;
+    uint64_t s = seed, got = 0;
+    while (got < count) {
+        const uint64_t v = xs_below(&s, n);
+        if (bits[v >> 6] & (1ull << (v & 63))) continue;
+        bits[v >> 6] |= 1ull << (v & 63);
+        ++got;
+    }
+    uint64_t w = 0;
+    for (uint64_t i = 0; i < n && w < count; ++i)
+        if (bits[i >> 6] & (1ull << (i & 63))) out[w++] = i;
+    free(bits);
+    return 0;
+}
