@@ -8,6 +8,7 @@
 #include <climits>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -172,27 +173,53 @@ ScratchU8 carve_scratch_u8(void* p, uint64_t q_count)
     return s;
 }
 
-template <int MT, int METRIC, class TopK>
+template <int MT, int BN, int NBUF, int SPLIT, int METRIC, class TopK>
 knng_gpu_status launch_u8_t(const CUtensorMap& mq, const CUtensorMap& mb, const KnnU8Params& p, cudaStream_t st)
 {
-    const SmemLayoutU8 L = smem_layout_u8(MT, p.kchunks, p.stages);
+    const SmemLayoutU8 L = smem_layout_u8(MT, BN, p.kchunks, p.stages, SPLIT, SPLIT > 1 ? TopK::kRegs / 2 : 0);
     const uint32_t smem = L.total + 1024;
-    auto kern = knn_u8_tc_kernel<MT, METRIC, TopK>;
+    auto kern = knn_u8_tc_kernel<MT, BN, NBUF, SPLIT, METRIC, TopK>;
     KNNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const uint32_t n_qtiles = (p.n_queries + MT * kTileRows - 1) / (MT * kTileRows);
     const uint32_t grid = std::min<uint32_t>(n_qtiles, static_cast<uint32_t>(sm_count()));
-    kern<<<grid, 64 + 128 * MT, smem, st>>>(mq, mb, p);
+    kern<<<grid, 64 + 128 * MT * SPLIT, smem, st>>>(mq, mb, p);
     KNNG_CUDA(cudaGetLastError());
     return KNNG_GPU_OK;
 }
 
-template <int MT, int METRIC>
-knng_gpu_status launch_u8_k(const CUtensorMap& mq, const CUtensorMap& mb, const KnnU8Params& p, cudaStream_t st)
+template <int MT, int BN, int NBUF, int METRIC>
+knng_gpu_status launch_u8_k(const CUtensorMap& mq, const CUtensorMap& mb, const KnnU8Params& p, int split,
+                            cudaStream_t st)
 {
-    if (p.k <= 16) return launch_u8_t<MT, METRIC, RegTopK<16>>(mq, mb, p, st);
-    if (p.k <= 32) return launch_u8_t<MT, METRIC, RegTopK<32>>(mq, mb, p, st);
-    if (p.k <= 128) return launch_u8_t<MT, METRIC, HeapTopK<128>>(mq, mb, p, st);
-    return launch_u8_t<MT, METRIC, HeapTopK<KNNG_GPU_MAX_K>>(mq, mb, p, st);
+    if (p.k <= 16 && split == 2) return launch_u8_t<MT, BN, NBUF, 2, METRIC, RegTopK<16>>(mq, mb, p, st);
+    if (p.k <= 16) return launch_u8_t<MT, BN, NBUF, 1, METRIC, RegTopK<16>>(mq, mb, p, st);
+    if (p.k <= 32) return launch_u8_t<MT, BN, NBUF, 1, METRIC, RegTopK<32>>(mq, mb, p, st);
+    if (p.k <= 128) return launch_u8_t<MT, BN, NBUF, 1, METRIC, HeapTopK<128>>(mq, mb, p, st);
+    return launch_u8_t<MT, BN, NBUF, 1, METRIC, HeapTopK<KNNG_GPU_MAX_K>>(mq, mb, p, st);
+}
+
+// Tile shapes of the fused kernel: (query tiles per CTA, base rows per tile,
+// TMEM accumulator buffers).
+struct TileShape {
+    int mt, bn, nbuf, split;
+};
+
+template <int MT, int BN, int NBUF>
+knng_gpu_status launch_u8_m(const CUtensorMap& mq, const CUtensorMap& mb, const KnnU8Params& p, int metric,
+                            int split, cudaStream_t st)
+{
+    return metric == 0 ? launch_u8_k<MT, BN, NBUF, 0>(mq, mb, p, split, st)
+                       : launch_u8_k<MT, BN, NBUF, 1>(mq, mb, p, split, st);
+}
+
+knng_gpu_status launch_u8(const CUtensorMap& mq, const CUtensorMap& mb, const KnnU8Params& p, TileShape ts,
+                          int metric, cudaStream_t st)
+{
+    if (ts.mt == 2 && ts.bn == 128) return launch_u8_m<2, 128, 2>(mq, mb, p, metric, ts.split, st);
+    if (ts.mt == 2 && ts.bn == 256) return launch_u8_m<2, 256, 1>(mq, mb, p, metric, 1, st);
+    if (ts.mt == 1 && ts.bn == 256) return launch_u8_m<1, 256, 2>(mq, mb, p, metric, 1, st);
+    if (ts.mt == 1 && ts.nbuf == 4) return launch_u8_m<1, 128, 4>(mq, mb, p, metric, 1, st);
+    return launch_u8_m<1, 128, 2>(mq, mb, p, metric, 1, st);
 }
 
 template <int METRIC, class TopK, class T>
@@ -292,16 +319,24 @@ knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_
         p.fallback_rows = sc.fallback_rows;
         p.fallback_count = sc.counters;
         p.error = reinterpret_cast<int*>(sc.counters + 1);
-        const int mt = p.kchunks <= 2 ? 2 : 1;
-        const uint32_t fixed = smem_layout_u8(mt, p.kchunks, 0).total + 1024;
+        if (const char* dbg = std::getenv("KNNG_GPU_DEBUG_FLAGS")) p.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
+        TileShape ts = p.kchunks <= 2 ? TileShape{2, 128, 2, 1} : TileShape{1, 128, 2, 1};
+        if (const char* tv = std::getenv("KNNG_GPU_TILE")) {
+            const int v = std::atoi(tv);
+            if (v == 1 && p.kchunks <= 2) ts = TileShape{2, 256, 1, 1};
+            if (v == 2) ts = TileShape{1, 256, 2, 1};
+            if (v == 3) ts = TileShape{1, 128, 2, 1};
+            if (v == 4) ts = TileShape{1, 128, 4, 1};
+            if (v == 6 && p.kchunks <= 2 && p.k <= 16) ts = TileShape{2, 128, 2, 2};
+        }
+        const uint32_t fixed = smem_layout_u8(ts.mt, ts.bn, p.kchunks, 0, ts.split, ts.split > 1 ? 16 : 0).total + 1024;
         const uint32_t budget = 227u * 1024u;
-        p.stages = std::min<uint32_t>(8, (budget - fixed) / kTileBytes);
-        if (p.stages < 2) return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: shared memory budget exceeded");
-        knng_gpu_status s;
-        if (mt == 2)
-            s = metric == 0 ? launch_u8_k<2, 0>(mq, mb, p, st) : launch_u8_k<2, 1>(mq, mb, p, st);
-        else
-            s = metric == 0 ? launch_u8_k<1, 0>(mq, mb, p, st) : launch_u8_k<1, 1>(mq, mb, p, st);
+        const uint32_t stage_bytes = (ts.bn / kTileRows) * kBoxBytes;
+        p.stages = std::min<uint32_t>(16, (budget - fixed) / stage_bytes);
+        if (const char* sv = std::getenv("KNNG_GPU_STAGES")) p.stages = std::min<uint32_t>(p.stages, std::atoi(sv));
+        if (p.stages < 2 || (ts.mt > 1 && p.stages < p.kchunks))
+            return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: shared memory budget exceeded");
+        knng_gpu_status s = launch_u8(mq, mb, p, ts, metric, st);
         KNNG_TRY(s);
         tk.stop(st);
         // Rows whose fp32 sums may round: recompute exactly (device-side

@@ -56,6 +56,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
     return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Same bound as mbar_wait, polling with the non-suspending test_wait (for
+// the single-thread producer / MMA roles, where wake-up latency matters).
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort)
+{
+    if (mbar_test_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if ((it & 1023u) == 0) {
+            if (*abort) return false;
+            if (clock64() - t0 > kSpinLimitCycles) return false;
+        }
+    }
+}
+
 // Wait for the phase with the given parity to complete. Returns false after
 // kSpinLimitCycles, or early when *abort becomes non-zero.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort)
@@ -143,7 +171,7 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar)
 
 // 32 lanes x 32 consecutive 32-bit columns: thread t of the warp receives
 // lane (base lane + t), columns [col, col+32).
-__device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, int32_t (&v)[32])
+__device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, int32_t* v)
 {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -157,11 +185,12 @@ __device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, int32_t (&v)[32])
         : "memory");
 }
 
-// Wait for outstanding tcgen05.ld; the registers are tied in so the compiler
-// cannot hoist their uses above the wait.
-__device__ __forceinline__ void tmem_ld_wait(int32_t (&v)[32])
+// Wait for outstanding tcgen05.ld. The destination registers are tied to
+// volatile asm statements placed after the wait, so the compiler cannot hoist
+// their uses above it.
+__device__ __forceinline__ void tie32(int32_t* v)
 {
-    asm volatile("tcgen05.wait::ld.sync.aligned;"
+    asm volatile(""
                  : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
                    "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]),
                    "+r"(v[15]), "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]),
@@ -169,6 +198,14 @@ __device__ __forceinline__ void tmem_ld_wait(int32_t (&v)[32])
                    "+r"(v[29]), "+r"(v[30]), "+r"(v[31])
                  :
                  : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_wait_n(int32_t* v)
+{
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < N; i += 32) tie32(v + i);
 }
 
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthreads)

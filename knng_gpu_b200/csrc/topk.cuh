@@ -35,6 +35,7 @@ __device__ __forceinline__ float key_to_float(int32_t key)
 // slot KCAP-1 and the threshold read is a static register.
 template <int KCAP>
 struct RegTopK {
+    static constexpr int kRegs = 2 * KCAP;
     int32_t key[KCAP];
     uint32_t id[KCAP];
 
@@ -92,6 +93,7 @@ struct RegTopK {
 // is the worst retained entry. Used where k does not fit in registers.
 template <int KMAX>
 struct HeapTopK {
+    static constexpr int kRegs = 4;
     int32_t hk[KMAX];
     uint32_t hi[KMAX];
     uint32_t size;
