@@ -112,6 +112,30 @@ knng_gpu_status knng_gpu_knn_f32(const float* d_x, uint64_t n, uint64_t d, uint6
                                  uint64_t k, int metric, uint32_t* d_ids, float* d_dists, void* stream,
                                  knng_gpu_stats* stats);
 
+/* ---- allocation-free variant of knng_gpu_knn_u8 -------------------------
+ * No counterpart in the reference (it has no GPU code). For callers that may
+ * not allocate device memory at all -- code running under a custom or
+ * pre-reserved memory pool, inside a host that forbids cudaMalloc after
+ * start-up, or a plugin that only receives device pointers from its host --
+ * and therefore cannot provide the `d_scratch` buffer knng_gpu_knn_u8 needs.
+ * Same arguments, semantics and output as knng_gpu_knn_u8 minus the scratch:
+ * the fallback-row list and counters live in a fixed device array built into
+ * the library (4 MiB + 256 B, held on every GPU that loads the library until
+ * the process exits). Limits and caveats:
+ *   - q_count must be <= KNNG_GPU_NOALLOC_MAX_QUERIES, else
+ *     KNNG_GPU_INVALID_ARGUMENT;
+ *   - the first call on a device looks up the array's device address (once
+ *     per device, with that device current); make that first call before any
+ *     stream capture;
+ *   - all calls share the one array: calls that overlap on the GPU (other
+ *     streams, other host threads) race and must be serialised by the caller.
+ * The call allocates nothing: no cudaMalloc/cudaFree and no allocating
+ * library routine. */
+#define KNNG_GPU_NOALLOC_MAX_QUERIES (1u << 20)
+knng_gpu_status knng_gpu_knn_u8_noalloc(const uint8_t* d_packed, const int32_t* d_norms, uint64_t n, uint64_t d,
+                                        uint64_t q_begin, uint64_t q_count, uint64_t k, int metric, uint32_t* d_ids,
+                                        float* d_dists, void* stream, knng_gpu_stats* stats);
+
 #ifdef __cplusplus
 }
 #endif

@@ -27,6 +27,7 @@ GPU_SYMBOLS = (
     "knng_gpu_knn_scratch_bytes",
     "knng_gpu_knn_u8",
     "knng_gpu_knn_f32",
+    "knng_gpu_knn_u8_noalloc",
 )
 
 
@@ -80,6 +81,11 @@ def gpu_lib() -> ctypes.CDLL:
                 c_int,
                 [c_void_p, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_int, c_void_p, c_void_p,
                  c_void_p, c_uint64, c_void_p, st],
+            ),
+            "knng_gpu_knn_u8_noalloc": (
+                c_int,
+                [c_void_p, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_int, c_void_p, c_void_p,
+                 c_void_p, st],
             ),
             "knng_gpu_knn_f32": (
                 c_int,

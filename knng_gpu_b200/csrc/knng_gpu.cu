@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "knn_exact.cuh"
@@ -494,6 +495,36 @@ knng_gpu_status device_pipeline(const float* x, uint64_t n, uint64_t d, uint64_t
 
 }  // namespace
 
+// ------------------------------------------------------------------ no-alloc scratch
+// Scratch of knng_gpu_knn_u8_noalloc: the fallback-row list for up to
+// KNNG_GPU_NOALLOC_MAX_QUERIES queries plus the counters. Host code must not
+// pass `g_noalloc_scratch` itself to a kernel (on the host it names a host
+// stand-in); noalloc_scratch_ptr() resolves the device address once per device.
+constexpr uint64_t kNoAllocScratchBytes = (static_cast<uint64_t>(KNNG_GPU_NOALLOC_MAX_QUERIES) * 4 + 255) / 256 * 256 + 256;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+knng_gpu_status noalloc_scratch_ptr(void** out)
+{
+    int dev = 0;
+    KNNG_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: device index out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_ptr[dev]) {
+        void* ptr = nullptr;
+        // The current device is `dev`, so this resolves that device's copy.
+        KNNG_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+        g_noalloc_ptr[dev] = ptr;
+    }
+    *out = g_noalloc_ptr[dev];
+    return KNNG_GPU_OK;
+}
+}  // namespace
+
 extern "C" {
 
 const char* knng_gpu_last_error(void) { return g_last_error.c_str(); }
@@ -596,6 +627,24 @@ knng_gpu_status knng_gpu_brute_force(const float* data, uint64_t n, uint64_t d, 
     }
     cleanup();
     return s;
+}
+
+knng_gpu_status knng_gpu_knn_u8_noalloc(const uint8_t* d_packed, const int32_t* d_norms, uint64_t n, uint64_t d,
+                                        uint64_t q_begin, uint64_t q_count, uint64_t k, int metric, uint32_t* d_ids,
+                                        float* d_dists, void* stream, knng_gpu_stats* stats)
+{
+    g_last_error.clear();
+    KNNG_TRY(validate(n, d, k, metric));
+    if (q_count > KNNG_GPU_NOALLOC_MAX_QUERIES)
+        return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: knng_gpu_knn_u8_noalloc handles at most " +
+                                                   std::to_string(KNNG_GPU_NOALLOC_MAX_QUERIES) +
+                                                   " queries per call (got " + std::to_string(q_count) + ")");
+    void* scratch = nullptr;
+    KNNG_TRY(noalloc_scratch_ptr(&scratch));
+    // knn_u8_impl zeroes the counters on `stream` before the kernel runs, so
+    // the previous call's contents never leak into this one.
+    return knn_u8_impl(d_packed, d_norms, n, d, q_begin, q_count, k, metric, d_ids, d_dists, scratch,
+                       kNoAllocScratchBytes, static_cast<cudaStream_t>(stream), stats);
 }
 
 }  // extern "C"
