@@ -1,0 +1,200 @@
+// GoogleTest-style tests of knng::gpu::brute_force_knn (include/knng/gpu/brute_force.hpp),
+// mirroring the reference's tests/brute_force_test.cpp case for case, plus
+// GPU-vs-CPU parity against the reference's own header template
+// knng::cpu::brute_force_knn. gtest is not installed on this image, so a
+// minimal TEST/EXPECT harness stands in; the bodies read like the reference's.
+// Built by tests/cpp/build.py against the reference's include/; run by
+// tests/test_cpp_dropin.py on a GPU.
+#include <array>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "knng/core/dataset.hpp"
+#include "knng/core/distance.hpp"
+#include "knng/core/graph.hpp"
+#include "knng/cpu/brute_force.hpp"
+#include "knng/gpu/brute_force.hpp"
+#include "knng/random.hpp"
+
+namespace {
+struct Registry {
+    std::vector<std::pair<std::string, std::function<void()>>> tests;
+    static Registry& get()
+    {
+        static Registry r;
+        return r;
+    }
+};
+int g_failures = 0;
+struct Reg {
+    Reg(const char* name, std::function<void()> f) { Registry::get().tests.emplace_back(name, std::move(f)); }
+};
+}  // namespace
+
+#define TEST(suite, name)                                              \
+    static void suite##_##name();                                      \
+    static Reg reg_##suite##_##name(#suite "." #name, suite##_##name); \
+    static void suite##_##name()
+#define EXPECT_TRUE(c)                                                                    \
+    do {                                                                                  \
+        if (!(c)) {                                                                       \
+            std::fprintf(stderr, "  %s:%d: EXPECT failed: %s\n", __FILE__, __LINE__, #c); \
+            ++g_failures;                                                                 \
+        }                                                                                 \
+    } while (0)
+#define EXPECT_EQ(a, b) EXPECT_TRUE((a) == (b))
+#define EXPECT_NE(a, b) EXPECT_TRUE((a) != (b))
+#define EXPECT_LE(a, b) EXPECT_TRUE((a) <= (b))
+#define EXPECT_FLOAT_EQ(a, b) EXPECT_TRUE(std::fabs(static_cast<double>(a) - static_cast<double>(b)) <= 1e-6)
+#define EXPECT_THROW(stmt, exc)       \
+    do {                              \
+        bool thrown_ = false;         \
+        try {                         \
+            stmt;                     \
+        } catch (const exc&) {        \
+            thrown_ = true;           \
+        } catch (...) {               \
+        }                             \
+        EXPECT_TRUE(thrown_ && #exc); \
+    } while (0)
+
+namespace {
+knng::Dataset two_clusters_eight_points()
+{
+    knng::Dataset ds(8, 2);
+    constexpr std::array<std::array<float, 2>, 8> coords{
+        {{0.0f, 0.0f}, {1.0f, 0.0f}, {0.0f, 1.0f}, {1.0f, 1.0f}, {4.0f, 4.0f}, {5.0f, 4.0f}, {4.0f, 5.0f}, {5.0f, 5.0f}}};
+    for (std::size_t i = 0; i < coords.size(); ++i) {
+        ds.row(i)[0] = coords[i][0];
+        ds.row(i)[1] = coords[i][1];
+    }
+    return ds;
+}
+
+knng::Dataset synthetic(std::size_t n, std::size_t d, std::uint64_t seed, bool integers)
+{
+    knng::Dataset ds(n, d);
+    knng::random::XorShift64 rng(seed);
+    for (auto& v : ds.data)
+        v = integers ? static_cast<float>(rng.next_below(256)) : 2.0f * rng.next_float01() - 1.0f;
+    return ds;
+}
+
+template <class D>
+void expect_identical(const knng::Dataset& ds, std::size_t k)
+{
+    const knng::Knng c = knng::cpu::brute_force_knn(ds, k, D{});
+    const knng::Knng g = knng::gpu::brute_force_knn(ds, k, D{});
+    EXPECT_EQ(g.n, c.n);
+    EXPECT_EQ(g.k, c.k);
+    EXPECT_TRUE(g.neighbors == c.neighbors);
+    EXPECT_TRUE(std::memcmp(g.distances.data(), c.distances.data(), c.distances.size() * sizeof(float)) == 0);
+}
+}  // namespace
+
+TEST(BruteForceKnnGpu, OutputShapeMatchesArguments)
+{
+    const auto g = knng::gpu::brute_force_knn(two_clusters_eight_points(), std::size_t{3}, knng::L2Squared{});
+    EXPECT_EQ(g.n, std::size_t{8});
+    EXPECT_EQ(g.k, std::size_t{3});
+    EXPECT_EQ(g.neighbors.size(), std::size_t{24});
+    EXPECT_EQ(g.distances.size(), std::size_t{24});
+}
+
+TEST(BruteForceKnnGpu, EightPointClusterHandVerifiedRows)
+{
+    const auto g = knng::gpu::brute_force_knn(two_clusters_eight_points(), std::size_t{3}, knng::L2Squared{});
+    EXPECT_EQ(g.neighbors_of(0)[0], 1u);
+    EXPECT_EQ(g.neighbors_of(0)[1], 2u);
+    EXPECT_EQ(g.neighbors_of(0)[2], 3u);
+    EXPECT_FLOAT_EQ(g.distances_of(0)[0], 1.0f);
+    EXPECT_FLOAT_EQ(g.distances_of(0)[1], 1.0f);
+    EXPECT_FLOAT_EQ(g.distances_of(0)[2], 2.0f);
+    EXPECT_EQ(g.neighbors_of(7)[0], 5u);
+    EXPECT_EQ(g.neighbors_of(7)[1], 6u);
+    EXPECT_EQ(g.neighbors_of(7)[2], 4u);
+    EXPECT_EQ(g.neighbors_of(4)[0], 5u);
+    EXPECT_EQ(g.neighbors_of(4)[1], 6u);
+    EXPECT_EQ(g.neighbors_of(4)[2], 7u);
+}
+
+TEST(BruteForceKnnGpu, SelfIsNeverANeighbor)
+{
+    const auto g = knng::gpu::brute_force_knn(two_clusters_eight_points(), std::size_t{5}, knng::L2Squared{});
+    for (std::size_t q = 0; q < g.n; ++q)
+        for (auto id : g.neighbors_of(q)) EXPECT_NE(static_cast<std::size_t>(id), q);
+}
+
+TEST(BruteForceKnnGpu, RowsAreSortedAscendingByDistance)
+{
+    const auto g = knng::gpu::brute_force_knn(two_clusters_eight_points(), std::size_t{5}, knng::L2Squared{});
+    for (std::size_t q = 0; q < g.n; ++q) {
+        const auto d = g.distances_of(q);
+        for (std::size_t j = 1; j < d.size(); ++j) EXPECT_LE(d[j - 1], d[j]);
+    }
+}
+
+TEST(BruteForceKnnGpu, KEqualsOneReturnsTheSingleClosest)
+{
+    const auto g = knng::gpu::brute_force_knn(two_clusters_eight_points(), std::size_t{1}, knng::L2Squared{});
+    EXPECT_EQ(g.neighbors_of(0)[0], 1u);
+    EXPECT_EQ(g.neighbors_of(3)[0], 1u);
+    EXPECT_EQ(g.neighbors_of(7)[0], 5u);
+}
+
+TEST(BruteForceKnnGpu, NegativeInnerProductMatchesCpu)
+{
+    expect_identical<knng::NegativeInnerProduct>(two_clusters_eight_points(), 3);
+}
+
+TEST(BruteForceKnnGpu, ZeroKThrowsInvalidArgument)
+{
+    EXPECT_THROW(knng::gpu::brute_force_knn(two_clusters_eight_points(), std::size_t{0}, knng::L2Squared{}),
+                 std::invalid_argument);
+}
+
+TEST(BruteForceKnnGpu, KGreaterThanNMinusOneThrowsInvalidArgument)
+{
+    EXPECT_THROW(knng::gpu::brute_force_knn(two_clusters_eight_points(), std::size_t{8}, knng::L2Squared{}),
+                 std::invalid_argument);
+}
+
+TEST(BruteForceKnnGpu, EmptyDatasetThrowsInvalidArgument)
+{
+    const knng::Dataset ds;
+    EXPECT_THROW(knng::gpu::brute_force_knn(ds, std::size_t{1}, knng::L2Squared{}), std::invalid_argument);
+}
+
+TEST(BruteForceKnnGpu, MatchesCpuOnIntegerData)
+{
+    expect_identical<knng::L2Squared>(synthetic(1500, 128, 42, true), 10);
+    expect_identical<knng::NegativeInnerProduct>(synthetic(900, 200, 43, true), 16);
+}
+
+TEST(BruteForceKnnGpu, MatchesCpuOnFloatData)
+{
+    expect_identical<knng::L2Squared>(synthetic(1024, 128, 42, false), 10);
+    expect_identical<knng::NegativeInnerProduct>(synthetic(700, 64, 44, false), 7);
+}
+
+int main()
+{
+    for (auto& [name, fn] : Registry::get().tests) {
+        const int before = g_failures;
+        try {
+            fn();
+        } catch (const std::exception& e) {
+            std::fprintf(stderr, "  unexpected exception: %s\n", e.what());
+            ++g_failures;
+        }
+        std::printf("[%s] %s\n", g_failures == before ? "  OK  " : " FAIL ", name.c_str());
+    }
+    std::printf("%zu tests, %d failed expectations\n", Registry::get().tests.size(), g_failures);
+    return g_failures == 0 ? 0 : 1;
+}
