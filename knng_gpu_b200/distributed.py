@@ -46,6 +46,27 @@ def slice_rows(global_n: int, num_ranks: int) -> int:
     return (global_n + num_ranks - 1) // num_ranks
 
 
+def gather_shards(local: torch.Tensor, n: int, world: int, group=None) -> torch.Tensor:
+    """All-gather each rank's ``compute_shard`` rows (padded to the largest
+    shard so the collective has equal chunks) and return the (n, ...) rows
+    in global order on every rank."""
+    max_shard = compute_shard(n, world, world - 1).count
+    if local.shape[0] != max_shard:
+        pad = torch.zeros((max_shard - local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
+                          device=local.device)
+        local = torch.cat([local, pad], 0)
+    out = torch.empty((world * max_shard,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+    return unpad_shards(out, n, world)
+
+
+def unpad_shards(t: torch.Tensor, n: int, world: int) -> torch.Tensor:
+    """Drop the padding rows of a gathered (world * max_shard, ...) tensor."""
+    max_shard = compute_shard(n, world, world - 1).count
+    parts = [t[r * max_shard: r * max_shard + compute_shard(n, world, r).count] for r in range(world)]
+    return torch.cat(parts, 0)
+
+
 class ShardedBuilder:
     """Reusable buffers for repeated sharded builds of an (n, d) dataset with k
     neighbours on this rank's GPU. All collectives run on the current stream."""
@@ -115,8 +136,4 @@ class ShardedBuilder:
         return self._unpad(self.all_ids), self._unpad(self.all_dists)
 
     def _unpad(self, t: torch.Tensor) -> torch.Tensor:
-        parts = []
-        for r in range(self.world):
-            c = compute_shard(self.n, self.world, r).count
-            parts.append(t[r * self.max_shard: r * self.max_shard + c])
-        return torch.cat(parts, 0)
+        return unpad_shards(t, self.n, self.world)
