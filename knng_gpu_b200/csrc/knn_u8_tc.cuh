@@ -116,6 +116,14 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
     int32_t* sMerge = reinterpret_cast<int32_t*>(smem + L.merge_off);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 46);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 47);
+    // Base tiles whose MMAs are known complete (published by one epilogue
+    // thread after its handoff wait). The producer reuses a B stage once the
+    // tile that read it is counted here, so the MMA warp issues one
+    // tcgen05.commit per tile (the TMEM handoff) instead of two.
+    volatile uint32_t* tiles_done = reinterpret_cast<volatile uint32_t*>(bars + 48);
+    // With fewer stages than two tiles' worth of K chunks a tile cannot wait
+    // for a whole earlier tile, so stages are released per chunk instead.
+    const bool stage_commits = p.stages < 2 * p.kchunks;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -138,6 +146,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
             mbar_init(&merge_empty[m], 4);
         }
         *abort_flag = 0;
+        *tiles_done = 0;
         fence_barrier_init();
         prefetch_tensormap(&tmap_q);
         prefetch_tensormap(&tmap_b);
@@ -151,7 +160,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
-            uint32_t stage = 0, phase = 0, a_par = 0;
+            uint32_t stage = 0, phase = 0, a_par = 0, load_idx = 0;
             bool ok = true;
             for (uint32_t t = blockIdx.x; t < n_qtiles && ok; t += gridDim.x) {
                 ok = mbar_wait(a_empty, a_par ^ 1, abort_flag);
@@ -164,8 +173,16 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                                     p.query_row0 + (t * MT + mt) * kTileRows, a_full);
                 for (uint32_t j = 0; j < n_btiles && ok; ++j) {
                     for (uint32_t kc = 0; kc < p.kchunks; ++kc) {
-                        ok = mbar_wait(&empty[stage], phase ^ 1, abort_flag);
-                        if (!ok) break;
+                        if (stage_commits) {
+                            ok = mbar_wait(&empty[stage], phase ^ 1, abort_flag);
+                            if (!ok) break;
+                        } else if (load_idx >= S) {
+                            // The stage last held load (load_idx - S), part of
+                            // tile (load_idx - S) / kchunks.
+                            ok = spin_until_geq(tiles_done, (load_idx - S) / p.kchunks + 1, abort_flag);
+                            if (!ok) break;
+                        }
+                        ++load_idx;
                         mbar_arrive_expect_tx(&full[stage], kStageBytes);
 #pragma unroll
                         for (int bx = 0; bx < kBoxesPerStage; ++bx)
@@ -220,7 +237,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                                 for (int ks = 0; ks < kChunkBytes / 32; ++ks)
                                     umma_u8(d_tmem, umma_desc_sw128(as + ks * 32), umma_desc_sw128(bs + ks * 32),
                                             idesc, (kc | ks) != 0);
-                                if (mt == MT - 1) umma_commit(&empty[s]);
+                                if (stage_commits && mt == MT - 1) umma_commit(&empty[s]);
                             }
                             if (ok) umma_commit(&tfull[mt]);
                         }
@@ -244,7 +261,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                                     umma_u8(d_tmem, umma_desc_sw128(as + ks * 32), umma_desc_sw128(bs + ks * 32),
                                             idesc, (kc | ks) != 0);
                             }
-                            umma_commit(&empty[s]);
+                            if (stage_commits) umma_commit(&empty[s]);
                         }
                         if (ok) umma_commit(&tfull[buf]);
                     }
@@ -314,6 +331,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                 ok = mbar_wait(&tfull[hb], (acc_i / NBUF) & 1, abort_flag);
                 if (!ok) break;
                 tc_fence_after();
+                if (ew == (kPerMtBars ? 4 * (MT - 1) : 0) && lane == 0) *tiles_done = acc_i + 1;
                 const uint32_t tb =
                     tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + (buf * MT + mt) * BN;
                 const int4* nb4 = reinterpret_cast<const int4*>(nbuf + (j & 1) * BN);

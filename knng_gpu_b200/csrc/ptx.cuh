@@ -99,6 +99,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// Bounded wait until a shared-memory counter reaches `target`.
+__device__ __forceinline__ bool spin_until_geq(volatile uint32_t* counter, uint32_t target, volatile int* abort)
+{
+    if (*counter >= target) return true;
+    const long long t0 = clock64();
+    for (uint32_t it = 1;; ++it) {
+        if (*counter >= target) return true;
+        if ((it & 255u) == 0) {
+            if (*abort) return false;
+            if (clock64() - t0 > kSpinLimitCycles) return false;
+        }
+        __nanosleep(32);
+    }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y,
                                             uint64_t* bar)
