@@ -78,6 +78,23 @@ __host__ __device__ inline SmemLayoutU8 smem_layout_u8(int mt, int bn, uint32_t 
     return L;
 }
 
+// Balanced three-way minimum tree over N registers (compile-time shape, so
+// the operands stay in registers).
+template <int N>
+__device__ __forceinline__ int32_t tree_min(const int32_t* v)
+{
+    if constexpr (N == 1) {
+        return v[0];
+    } else if constexpr (N == 2) {
+        return min(v[0], v[1]);
+    } else if constexpr (N == 3) {
+        return __vimin3_s32(v[0], v[1], v[2]);
+    } else {
+        constexpr int a = N / 3, b = (N - a) / 2, c = N - a - b;
+        return __vimin3_s32(tree_min<a>(v), tree_min<b>(v + a), tree_min<c>(v + a + b));
+    }
+}
+
 template <int MT, int BN, int NBUF, int SPLIT, int METRIC, class TopK>
 __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
     knn_u8_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_b,
@@ -337,80 +354,60 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                 const int4* nb4 = reinterpret_cast<const int4*>(nbuf + (j & 1) * BN);
                 // 32-column chunks, software-pipelined: the TMEM load of chunk
                 // c+1 is in flight while chunk c is filtered.
-                constexpr int kChunks = BN / 32 / SPLIT;
-                const uint32_t tbh = tb + half * kChunks * 32;
-                const int4* nb4h = nb4 + half * kChunks * 8;
-                // With SPLIT == 2 (four epilogue warps per SMSP) registers are
-                // scarce and warp parallelism hides the load latency instead.
-                constexpr bool kPipe = SPLIT == 1;
-                int32_t va[32], vb[kPipe ? 32 : 1];
-                __syncwarp();
-                if (kPipe && !(p.debug_flags & 4u)) {
-                    tmem_ld_32cols(tbh, va);
-                    tmem_ld_wait_n<32>(va);
-                }
+                // Steps of kW columns: one TMEM wait per step, all keys of the
+                // step computed before one threshold test (ILP over kW keys).
+                constexpr int kCols = BN / SPLIT;
+                constexpr int kW = SPLIT == 1 ? 64 : 32;
+                const uint32_t tbh = tb + half * kCols;
+                const int4* nb4h = nb4 + half * kCols / 4;
 #pragma unroll
-                for (int c = 0; c < kChunks; ++c) {
-                    int32_t* vc = (kPipe && (c & 1)) ? vb : va;
-                    int32_t* vn = (c & 1) ? va : vb;
-                    if (!kPipe) {
-                        __syncwarp();
-                        if (!(p.debug_flags & 4u)) {
-                            tmem_ld_32cols(tbh + c * 32, va);
-                            tmem_ld_wait_n<32>(va);
-                        }
-                        if (c + 1 == kChunks) {
-                            tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&tempty[hb]);
-                        }
-                    } else if (c + 1 < kChunks) {
-                        __syncwarp();
-                        if (!(p.debug_flags & 4u)) tmem_ld_32cols(tbh + (c + 1) * 32, vn);
-                    } else {
+                for (int st = 0; st < kCols / kW; ++st) {
+                    int32_t v[kW];
+                    __syncwarp();
+                    if (!(p.debug_flags & 4u)) {
+#pragma unroll
+                        for (int c = 0; c < kW / 32; ++c) tmem_ld_32cols(tbh + st * kW + c * 32, v + c * 32);
+                        tmem_ld_wait_n<kW>(v);
+                    }
+                    if (st + 1 == kCols / kW) {
                         // Every column of this buffer is in registers: hand it
                         // back to the MMA warp before the last filtering step.
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&tempty[hb]);
                     }
-                    if (!(p.debug_flags & 1u)) {
+                    if (p.debug_flags & 1u) continue;
 #pragma unroll
-                        for (int i4 = 0; i4 < 8; ++i4) {
-                            const int4 nn = nb4h[c * 8 + i4];
-                            if (METRIC == 0) {
-                                vc[4 * i4 + 0] = nn.x - 2 * vc[4 * i4 + 0];
-                                vc[4 * i4 + 1] = nn.y - 2 * vc[4 * i4 + 1];
-                                vc[4 * i4 + 2] = nn.z - 2 * vc[4 * i4 + 2];
-                                vc[4 * i4 + 3] = nn.w - 2 * vc[4 * i4 + 3];
-                            } else {
-                                vc[4 * i4 + 0] = nn.x - vc[4 * i4 + 0];
-                                vc[4 * i4 + 1] = nn.y - vc[4 * i4 + 1];
-                                vc[4 * i4 + 2] = nn.z - vc[4 * i4 + 2];
-                                vc[4 * i4 + 3] = nn.w - vc[4 * i4 + 3];
-                            }
+                    for (int i4 = 0; i4 < kW / 4; ++i4) {
+                        const int4 nn = nb4h[st * kW / 4 + i4];
+                        if (METRIC == 0) {
+                            v[4 * i4 + 0] = nn.x - 2 * v[4 * i4 + 0];
+                            v[4 * i4 + 1] = nn.y - 2 * v[4 * i4 + 1];
+                            v[4 * i4 + 2] = nn.z - 2 * v[4 * i4 + 2];
+                            v[4 * i4 + 3] = nn.w - 2 * v[4 * i4 + 3];
+                        } else {
+                            v[4 * i4 + 0] = nn.x - v[4 * i4 + 0];
+                            v[4 * i4 + 1] = nn.y - v[4 * i4 + 1];
+                            v[4 * i4 + 2] = nn.z - v[4 * i4 + 2];
+                            v[4 * i4 + 3] = nn.w - v[4 * i4 + 3];
                         }
-                        // Tree minimum (depth 3) instead of a serial chain.
-                        int32_t a[11];
+                    }
+                    const int32_t step_min = tree_min<kW>(v);  // depth log3(kW)
+                    if (step_min < thr && !(p.debug_flags & 2u)) {
+                        // Rare path, per 32 columns: spill the keys and insert
+                        // those under the running threshold, in id order.
 #pragma unroll
-                        for (int i = 0; i < 10; ++i) a[i] = __vimin3_s32(vc[3 * i], vc[3 * i + 1], vc[3 * i + 2]);
-                        a[10] = min(vc[30], vc[31]);
-                        const int32_t b0 = __vimin3_s32(a[0], a[1], a[2]);
-                        const int32_t b1 = __vimin3_s32(a[3], a[4], a[5]);
-                        const int32_t b2 = __vimin3_s32(a[6], a[7], a[8]);
-                        const int32_t b3 = min(a[9], a[10]);
-                        const int32_t m0 = __vimin3_s32(b0, b1, b2), m1 = b3;
-                        if (min(m0, m1) < thr && !(p.debug_flags & 2u)) {
-                            // Rare path: spill this chunk's keys and insert the
-                            // ones under the running threshold, in id order.
+                        for (int c = 0; c < kW / 32; ++c) {
+                            const int32_t* vc = v + c * 32;
                             uint32_t mask = 0;
 #pragma unroll
                             for (int i = 0; i < 32; ++i) mask |= (vc[i] < thr ? 1u : 0u) << i;
+                            if (!mask) continue;
 #pragma unroll
                             for (int i4 = 0; i4 < 8; ++i4)
                                 *reinterpret_cast<int4*>(slow + 4 * i4) =
                                     make_int4(vc[4 * i4], vc[4 * i4 + 1], vc[4 * i4 + 2], vc[4 * i4 + 3]);
-                            const uint32_t col0 = p.base_id0 + j * BN + (half * kChunks + c) * 32;
+                            const uint32_t col0 = p.base_id0 + j * BN + half * kCols + st * kW + c * 32;
                             while (mask) {
                                 const int i = __ffs(mask) - 1;
                                 mask &= mask - 1;
@@ -422,10 +419,6 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                                 }
                             }
                         }
-                    }
-                    if (kPipe && c + 1 < kChunks) {
-                        __syncwarp();
-                        if (!(p.debug_flags & 4u)) tmem_ld_wait_n<32>(vn);
                     }
                 }
             }

@@ -192,7 +192,8 @@ template <int MT, int BN, int NBUF, int METRIC>
 knng_gpu_status launch_u8_k(const CUtensorMap& mq, const CUtensorMap& mb, const KnnU8Params& p, int split,
                             cudaStream_t st)
 {
-    if (p.k <= 16 && split == 2) return launch_u8_t<MT, BN, NBUF, 2, METRIC, RegTopK<16>>(mq, mb, p, st);
+    (void)split;  // the column-split epilogue (SPLIT = 2) is not instantiated
+    if (p.k <= 10) return launch_u8_t<MT, BN, NBUF, 1, METRIC, RegTopK<10>>(mq, mb, p, st);
     if (p.k <= 16) return launch_u8_t<MT, BN, NBUF, 1, METRIC, RegTopK<16>>(mq, mb, p, st);
     if (p.k <= 32) return launch_u8_t<MT, BN, NBUF, 1, METRIC, RegTopK<32>>(mq, mb, p, st);
     if (p.k <= 128) return launch_u8_t<MT, BN, NBUF, 1, METRIC, HeapTopK<128>>(mq, mb, p, st);
@@ -216,10 +217,9 @@ knng_gpu_status launch_u8_m(const CUtensorMap& mq, const CUtensorMap& mb, const 
 knng_gpu_status launch_u8(const CUtensorMap& mq, const CUtensorMap& mb, const KnnU8Params& p, TileShape ts,
                           int metric, cudaStream_t st)
 {
-    if (ts.mt == 2 && ts.bn == 128) return launch_u8_m<2, 128, 2>(mq, mb, p, metric, ts.split, st);
-    if (ts.mt == 2 && ts.bn == 256) return launch_u8_m<2, 256, 1>(mq, mb, p, metric, 1, st);
-    if (ts.mt == 1 && ts.bn == 256) return launch_u8_m<1, 256, 2>(mq, mb, p, metric, 1, st);
-    if (ts.mt == 1 && ts.nbuf == 4) return launch_u8_m<1, 128, 4>(mq, mb, p, metric, 1, st);
+    // Measured alternatives (BN = 256 with one TMEM buffer, MT = 1 with four
+    // buffers, a two-way column split of the epilogue) were slower at d = 128.
+    if (ts.mt == 2) return launch_u8_m<2, 128, 2>(mq, mb, p, metric, 1, st);
     return launch_u8_m<1, 128, 2>(mq, mb, p, metric, 1, st);
 }
 
@@ -322,14 +322,6 @@ knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_
         p.error = reinterpret_cast<int*>(sc.counters + 1);
         if (const char* dbg = std::getenv("KNNG_GPU_DEBUG_FLAGS")) p.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
         TileShape ts = p.kchunks <= 2 ? TileShape{2, 128, 2, 1} : TileShape{1, 128, 2, 1};
-        if (const char* tv = std::getenv("KNNG_GPU_TILE")) {
-            const int v = std::atoi(tv);
-            if (v == 1 && p.kchunks <= 2) ts = TileShape{2, 256, 1, 1};
-            if (v == 2) ts = TileShape{1, 256, 2, 1};
-            if (v == 3) ts = TileShape{1, 128, 2, 1};
-            if (v == 4) ts = TileShape{1, 128, 4, 1};
-            if (v == 6 && p.kchunks <= 2 && p.k <= 16) ts = TileShape{2, 128, 2, 2};
-        }
         const uint32_t fixed = smem_layout_u8(ts.mt, ts.bn, p.kchunks, 0, ts.split, ts.split > 1 ? 16 : 0).total + 1024;
         const uint32_t budget = 227u * 1024u;
         const uint32_t stage_bytes = (ts.bn / kTileRows) * kBoxBytes;
