@@ -70,10 +70,16 @@ int knng_gpu_device_count(void);
  * (include/knng/cpu/brute_force.hpp:336-376). `data` is the row-major
  * n x d fp32 payload of a knng::Dataset (dataset.hpp:76-152, data_ptr()),
  * `ids`/`dists` are caller-allocated n*k arrays (Knng::neighbors/distances).
- * Runs on the current CUDA device; allocates and frees its device memory
- * inside the call. `stats` may be NULL. */
+ * Runs on the current CUDA device. Device buffers are cached per device and
+ * reused by later calls (see knng_gpu_release_cached_buffers); calls on one
+ * device are serialised. `stats` may be NULL. */
 knng_gpu_status knng_gpu_brute_force(const float* data, uint64_t n, uint64_t d, uint64_t k, int metric,
                                      uint32_t* ids, float* dists, knng_gpu_stats* stats);
+
+/* Free the device buffers and stream that knng_gpu_brute_force keeps per
+ * device between calls (they are grown on demand and otherwise held until
+ * process exit). No counterpart in the reference. */
+void knng_gpu_release_cached_buffers(void);
 
 /* ---- device-resident API (inputs already in HBM) ------------------------
  * All pointers are device pointers; `stream` is a cudaStream_t (NULL = the

@@ -20,6 +20,7 @@ GPU_SYMBOLS = (
     "knng_gpu_last_error",
     "knng_gpu_device_count",
     "knng_gpu_brute_force",
+    "knng_gpu_release_cached_buffers",
     "knng_gpu_workspace_bytes",
     "knng_gpu_brute_force_device",
     "knng_gpu_padded_dim",
@@ -69,6 +70,7 @@ def gpu_lib() -> ctypes.CDLL:
             "knng_gpu_last_error": (c_char_p, []),
             "knng_gpu_device_count": (c_int, []),
             "knng_gpu_brute_force": (c_int, [c_void_p, c_uint64, c_uint64, c_uint64, c_int, c_void_p, c_void_p, st]),
+            "knng_gpu_release_cached_buffers": (None, []),
             "knng_gpu_workspace_bytes": (c_uint64, [c_uint64, c_uint64]),
             "knng_gpu_brute_force_device": (
                 c_int,

@@ -517,6 +517,32 @@ knng_gpu_status noalloc_scratch_ptr(void** out)
 }
 }  // namespace
 
+// ------------------------------------------------------------------ host-API buffer cache
+// knng_gpu_brute_force keeps its device buffers and stream per device between
+// calls (grown on demand, freed by knng_gpu_release_cached_buffers), so a
+// build pays no cudaMalloc/cudaFree once the sizes have been seen.
+namespace {
+struct HostCache {
+    std::mutex mutex;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    void *x = nullptr, *ids = nullptr, *dists = nullptr, *ws = nullptr;
+    uint64_t x_cap = 0, ids_cap = 0, dists_cap = 0, ws_cap = 0;
+};
+HostCache g_host_cache[kMaxDevices];
+
+knng_gpu_status grow(void** ptr, uint64_t* cap, uint64_t need)
+{
+    if (*cap >= need && *ptr) return KNNG_GPU_OK;
+    if (*ptr) cudaFree(*ptr);
+    *ptr = nullptr;
+    *cap = 0;
+    KNNG_CUDA(cudaMalloc(ptr, need > 0 ? need : 256));
+    *cap = need;
+    return KNNG_GPU_OK;
+}
+}  // namespace
+
 extern "C" {
 
 const char* knng_gpu_last_error(void) { return g_last_error.c_str(); }
@@ -585,40 +611,50 @@ knng_gpu_status knng_gpu_brute_force(const float* data, uint64_t n, uint64_t d, 
         cudaGetLastError();
         return fail(KNNG_GPU_CUDA_ERROR, "knng::gpu::brute_force_knn: no CUDA device available");
     }
-    cudaStream_t st;
-    KNNG_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    int dev = 0;
+    KNNG_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: device index out of range");
+    HostCache& c = g_host_cache[dev];
+    std::lock_guard<std::mutex> lock(c.mutex);
+    c.device = dev;
+    if (!c.stream) KNNG_CUDA(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+    cudaStream_t st = c.stream;
     const uint64_t ws_bytes = knng_gpu_workspace_bytes(n, d);
-    float* dx = nullptr;
-    uint32_t* dids = nullptr;
-    float* ddist = nullptr;
-    void* ws = nullptr;
-    knng_gpu_status s = KNNG_GPU_OK;
-    auto cleanup = [&]() {
-        cudaFree(dx);
-        cudaFree(dids);
-        cudaFree(ddist);
-        cudaFree(ws);
-        cudaStreamDestroy(st);
-    };
-    auto step = [&](cudaError_t e, const char* what) {
-        if (e != cudaSuccess && s == KNNG_GPU_OK)
-            s = fail(e == cudaErrorMemoryAllocation ? KNNG_GPU_OUT_OF_MEMORY : KNNG_GPU_CUDA_ERROR,
-                     std::string("knng::gpu::brute_force_knn: ") + what + ": " + cudaGetErrorString(e));
-        return s == KNNG_GPU_OK;
-    };
-    if (step(cudaMalloc(&dx, n * d * sizeof(float)), "cudaMalloc") &&
-        step(cudaMalloc(&dids, n * k * sizeof(uint32_t)), "cudaMalloc") &&
-        step(cudaMalloc(&ddist, n * k * sizeof(float)), "cudaMalloc") && step(cudaMalloc(&ws, ws_bytes), "cudaMalloc") &&
-        step(cudaMemcpyAsync(dx, data, n * d * sizeof(float), cudaMemcpyHostToDevice, st), "H2D copy")) {
-        s = device_pipeline(dx, n, d, k, metric, dids, ddist, ws, ws_bytes, st, stats);
-        if (s == KNNG_GPU_OK) {
-            step(cudaMemcpyAsync(ids, dids, n * k * sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "D2H copy");
-            step(cudaMemcpyAsync(dists, ddist, n * k * sizeof(float), cudaMemcpyDeviceToHost, st), "D2H copy");
-            step(cudaStreamSynchronize(st), "synchronize");
-        }
+    KNNG_TRY(grow(&c.x, &c.x_cap, n * d * sizeof(float)));
+    KNNG_TRY(grow(&c.ids, &c.ids_cap, n * k * sizeof(uint32_t)));
+    KNNG_TRY(grow(&c.dists, &c.dists_cap, n * k * sizeof(float)));
+    KNNG_TRY(grow(&c.ws, &c.ws_cap, ws_bytes));
+    float* dx = static_cast<float*>(c.x);
+    uint32_t* dids = static_cast<uint32_t*>(c.ids);
+    float* ddist = static_cast<float*>(c.dists);
+    KNNG_CUDA(cudaMemcpyAsync(dx, data, n * d * sizeof(float), cudaMemcpyHostToDevice, st));
+    KNNG_TRY(device_pipeline(dx, n, d, k, metric, dids, ddist, c.ws, c.ws_cap, st, stats));
+    KNNG_CUDA(cudaMemcpyAsync(ids, dids, n * k * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    KNNG_CUDA(cudaMemcpyAsync(dists, ddist, n * k * sizeof(float), cudaMemcpyDeviceToHost, st));
+    KNNG_CUDA(cudaStreamSynchronize(st));
+    return KNNG_GPU_OK;
+}
+
+void knng_gpu_release_cached_buffers(void)
+{
+    int cur = 0;
+    const bool have_cur = cudaGetDevice(&cur) == cudaSuccess;
+    for (int i = 0; i < kMaxDevices; ++i) {
+        HostCache& c = g_host_cache[i];
+        std::lock_guard<std::mutex> lock(c.mutex);
+        if (!c.stream && !c.x && !c.ws) continue;
+        cudaSetDevice(c.device);
+        cudaFree(c.x);
+        cudaFree(c.ids);
+        cudaFree(c.dists);
+        cudaFree(c.ws);
+        if (c.stream) cudaStreamDestroy(c.stream);
+        c.x = c.ids = c.dists = c.ws = nullptr;
+        c.x_cap = c.ids_cap = c.dists_cap = c.ws_cap = 0;
+        c.stream = nullptr;
     }
-    cleanup();
-    return s;
+    if (have_cur) cudaSetDevice(cur);
+    cudaGetLastError();
 }
 
 knng_gpu_status knng_gpu_knn_u8_noalloc(const uint8_t* d_packed, const int32_t* d_norms, uint64_t n, uint64_t d,
