@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(kExactThreads)
             const float dist = METRIC == 0 ? acc[b] : -acc[b];
             const int32_t key = ordered_key(dist);
             if (r < p.n_base && id != self_id && key < thr) {
-                tk.insert(key, id);
+                tk.insert_increasing(key, id);
                 thr = tk.thr();
             }
         }

@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                 // Steps of kW columns: one TMEM wait per step, all keys of the
                 // step computed before one threshold test (ILP over kW keys).
                 constexpr int kCols = BN / SPLIT;
-                constexpr int kW = SPLIT == 1 ? 64 : 32;
+                constexpr int kW = (SPLIT == 1 && TopK::kRegs <= 64) ? 64 : 32;
                 const uint32_t tbh = tb + half * kCols;
                 const int4* nb4h = nb4 + half * kCols / 4;
 #pragma unroll
@@ -414,7 +414,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                                 const int32_t key = slow[i];
                                 const uint32_t id = col0 + i;
                                 if (key < thr && id != self_id) {
-                                    tk.insert(key, id);
+                                    tk.insert_increasing(key, id);
                                     thr = tk.thr();
                                 }
                             }

@@ -196,6 +196,9 @@ knng_gpu_status launch_u8_k(const CUtensorMap& mq, const CUtensorMap& mb, const 
     if (p.k <= 10) return launch_u8_t<MT, BN, NBUF, 1, METRIC, RegTopK<10>>(mq, mb, p, st);
     if (p.k <= 16) return launch_u8_t<MT, BN, NBUF, 1, METRIC, RegTopK<16>>(mq, mb, p, st);
     if (p.k <= 32) return launch_u8_t<MT, BN, NBUF, 1, METRIC, RegTopK<32>>(mq, mb, p, st);
+    if constexpr (MT == 1) {
+        if (p.k <= 64) return launch_u8_t<MT, BN, NBUF, 1, METRIC, RegTopK<64>>(mq, mb, p, st);
+    }
     if (p.k <= 128) return launch_u8_t<MT, BN, NBUF, 1, METRIC, HeapTopK<128>>(mq, mb, p, st);
     return launch_u8_t<MT, BN, NBUF, 1, METRIC, HeapTopK<KNNG_GPU_MAX_K>>(mq, mb, p, st);
 }
@@ -321,7 +324,8 @@ knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_
         p.fallback_count = sc.counters;
         p.error = reinterpret_cast<int*>(sc.counters + 1);
         if (const char* dbg = std::getenv("KNNG_GPU_DEBUG_FLAGS")) p.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
-        TileShape ts = p.kchunks <= 2 ? TileShape{2, 128, 2, 1} : TileShape{1, 128, 2, 1};
+        // Two query tiles per CTA need k <= 32 (register budget of 320 threads).
+        TileShape ts = (p.kchunks <= 2 && k <= 32) ? TileShape{2, 128, 2, 1} : TileShape{1, 128, 2, 1};
         const uint32_t fixed = smem_layout_u8(ts.mt, ts.bn, p.kchunks, 0, ts.split, ts.split > 1 ? 16 : 0).total + 1024;
         const uint32_t budget = 227u * 1024u;
         const uint32_t stage_bytes = (ts.bn / kTileRows) * kBoxBytes;

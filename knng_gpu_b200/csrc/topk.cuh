@@ -69,6 +69,26 @@ struct RegTopK {
         }
     }
 
+    // Insert when ids arrive in increasing order (one thread scanning base
+    // rows in order): an equal key never displaces an earlier id, so only
+    // keys need comparing. Precondition: v < key[KCAP-1].
+    __device__ __forceinline__ void insert_increasing(int32_t v, uint32_t vid)
+    {
+#pragma unroll
+        for (int i = KCAP - 1; i > 0; --i) {
+            const bool shift = key[i - 1] > v;
+            const bool here = key[i] > v;
+            const int32_t nk = shift ? key[i - 1] : (here ? v : key[i]);
+            const uint32_t ni = shift ? id[i - 1] : (here ? vid : id[i]);
+            key[i] = nk;
+            id[i] = ni;
+        }
+        if (key[0] > v) {
+            key[0] = v;
+            id[0] = vid;
+        }
+    }
+
     // Entry j (0-based, ascending) of the k retained.
     template <class F>
     __device__ __forceinline__ void for_each(uint32_t k, F&& f) const
@@ -124,6 +144,8 @@ struct HeapTopK {
         }
         sift_down_from_root(v, vid, size);
     }
+
+    __device__ __forceinline__ void insert_increasing(int32_t v, uint32_t vid) { insert(v, vid); }
 
     __device__ void sift_down_from_root(int32_t v, uint32_t vid, uint32_t sz)
     {
