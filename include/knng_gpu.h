@@ -44,19 +44,21 @@ typedef enum {
  * (tools/build_knng.cpp:183-188): 0 = L2Squared, 1 = NegativeInnerProduct. */
 typedef enum { KNNG_METRIC_L2_SQUARED = 0, KNNG_METRIC_NEGATIVE_INNER_PRODUCT = 1 } knng_metric;
 
-/* Which kernel family produced the result. */
-typedef enum { KNNG_PATH_U8_TENSOR = 0, KNNG_PATH_F32_EXACT = 1 } knng_path;
+/* Which kernel family produced the result: exact u8 UMMA (integer data in
+ * [0,255]) or bf16x3 UMMA candidate filter + exact fp32 re-rank (other data). */
+typedef enum { KNNG_PATH_U8_TENSOR = 0, KNNG_PATH_F32_TENSOR = 1 } knng_path;
 
 #define KNNG_GPU_MAX_K 1024u
 
 typedef struct {
     int path;                 /* knng_path */
-    uint64_t fallback_rows;   /* u8-path rows recomputed by the exact kernel */
+    uint64_t fallback_rows;   /* rows recomputed by the exact fp32 kernel */
     float pack_ms;            /* integer check + u8 pack + row norms */
     float knn_ms;             /* fused KNN kernel (device time, CUDA events) */
     float fallback_ms;        /* exact kernel on fallback rows */
     float total_ms;           /* whole call, device time */
     uint32_t kernel_launches; /* kernels this call launched */
+    float f32_err_ratio;      /* fp32 path: max |approximate - exact| / proof margin seen (< 1) */
 } knng_gpu_stats;
 
 /* Message of the last failure on this thread ("" if none). */
@@ -87,7 +89,7 @@ void knng_gpu_release_cached_buffers(void);
  * workspace of at least knng_gpu_workspace_bytes(n, d) bytes, 256-byte
  * aligned. Same semantics and output layout as knng_gpu_brute_force; the
  * call synchronises `stream` once (to read which path applies). */
-uint64_t knng_gpu_workspace_bytes(uint64_t n, uint64_t d);
+uint64_t knng_gpu_workspace_bytes(uint64_t n, uint64_t d, uint64_t k);
 knng_gpu_status knng_gpu_brute_force_device(const float* d_data, uint64_t n, uint64_t d, uint64_t k, int metric,
                                             uint32_t* d_ids, float* d_dists, void* d_workspace,
                                             uint64_t workspace_bytes, void* stream, knng_gpu_stats* stats);
@@ -105,7 +107,11 @@ knng_gpu_status knng_gpu_brute_force_device(const float* d_data, uint64_t n, uin
  * knng_gpu_knn_u8: queries are packed rows [q_begin, q_begin+q_count) of the
  *   base; results for query row i go to row i of d_ids/d_dists (q_count x k).
  *   d_scratch: >= knng_gpu_knn_scratch_bytes(q_count) bytes.
- * knng_gpu_knn_f32: exact fp32 kernel on raw rows (any values). */
+ * knng_gpu_knn_f32: any fp32 data: bf16x3 tensor-core candidate filter over
+ *   all n rows, exact re-rank with the reference's arithmetic and a proven
+ *   error bound, exact kernel for rows the bound cannot certify.
+ *   d_scratch: >= knng_gpu_knn_f32_scratch_bytes(n, d, q_count, k) bytes,
+ *   256-byte aligned. */
 uint64_t knng_gpu_padded_dim(uint64_t d);
 knng_gpu_status knng_gpu_pack_u8(const float* d_x, uint64_t rows, uint64_t d, uint8_t* d_packed,
                                  int32_t* d_norms, int32_t* d_nonint, void* stream);
@@ -114,9 +120,10 @@ knng_gpu_status knng_gpu_knn_u8(const uint8_t* d_packed, const int32_t* d_norms,
                                 uint64_t q_begin, uint64_t q_count, uint64_t k, int metric, uint32_t* d_ids,
                                 float* d_dists, void* d_scratch, uint64_t scratch_bytes, void* stream,
                                 knng_gpu_stats* stats);
+uint64_t knng_gpu_knn_f32_scratch_bytes(uint64_t n, uint64_t d, uint64_t q_count, uint64_t k);
 knng_gpu_status knng_gpu_knn_f32(const float* d_x, uint64_t n, uint64_t d, uint64_t q_begin, uint64_t q_count,
-                                 uint64_t k, int metric, uint32_t* d_ids, float* d_dists, void* stream,
-                                 knng_gpu_stats* stats);
+                                 uint64_t k, int metric, uint32_t* d_ids, float* d_dists, void* d_scratch,
+                                 uint64_t scratch_bytes, void* stream, knng_gpu_stats* stats);
 
 /* ---- allocation-free variant of knng_gpu_knn_u8 -------------------------
  * No counterpart in the reference (it has no GPU code). For callers that may

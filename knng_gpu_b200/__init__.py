@@ -15,6 +15,7 @@ from .api import (  # noqa: F401
     brute_force_knn_device,
     device_count,
     knn_f32,
+    knn_f32_scratch_bytes,
     knn_scratch_bytes,
     knn_u8,
     pack_u8,

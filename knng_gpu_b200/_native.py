@@ -27,6 +27,7 @@ GPU_SYMBOLS = (
     "knng_gpu_pack_u8",
     "knng_gpu_knn_scratch_bytes",
     "knng_gpu_knn_u8",
+    "knng_gpu_knn_f32_scratch_bytes",
     "knng_gpu_knn_f32",
     "knng_gpu_knn_u8_noalloc",
 )
@@ -43,6 +44,7 @@ class KnngGpuStats(ctypes.Structure):
         ("fallback_ms", c_float),
         ("total_ms", c_float),
         ("kernel_launches", c_uint32),
+        ("f32_err_ratio", c_float),
     ]
 
     def as_dict(self) -> dict:
@@ -71,7 +73,8 @@ def gpu_lib() -> ctypes.CDLL:
             "knng_gpu_device_count": (c_int, []),
             "knng_gpu_brute_force": (c_int, [c_void_p, c_uint64, c_uint64, c_uint64, c_int, c_void_p, c_void_p, st]),
             "knng_gpu_release_cached_buffers": (None, []),
-            "knng_gpu_workspace_bytes": (c_uint64, [c_uint64, c_uint64]),
+            "knng_gpu_workspace_bytes": (c_uint64, [c_uint64, c_uint64, c_uint64]),
+            "knng_gpu_knn_f32_scratch_bytes": (c_uint64, [c_uint64, c_uint64, c_uint64, c_uint64]),
             "knng_gpu_brute_force_device": (
                 c_int,
                 [c_void_p, c_uint64, c_uint64, c_uint64, c_int, c_void_p, c_void_p, c_void_p, c_uint64, c_void_p, st],
@@ -91,7 +94,8 @@ def gpu_lib() -> ctypes.CDLL:
             ),
             "knng_gpu_knn_f32": (
                 c_int,
-                [c_void_p, c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_int, c_void_p, c_void_p, c_void_p, st],
+                [c_void_p, c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_int, c_void_p, c_void_p, c_void_p,
+                 c_uint64, c_void_p, st],
             ),
         }
         del f32p, u32p, i32p

@@ -160,8 +160,8 @@ def _stream_handle(stream) -> int | None:
     return int(stream.cuda_stream)
 
 
-def workspace_bytes(n: int, d: int) -> int:
-    return int(gpu_lib().knng_gpu_workspace_bytes(n, d))
+def workspace_bytes(n: int, d: int, k: int) -> int:
+    return int(gpu_lib().knng_gpu_workspace_bytes(n, d, k))
 
 
 def brute_force_knn_device(x, k: int, distance=L2Squared(), out_ids=None, out_dists=None, workspace=None,
@@ -170,7 +170,7 @@ def brute_force_knn_device(x, k: int, distance=L2Squared(), out_ids=None, out_di
 
     Returns ``(ids, dists, stats)`` as CUDA tensors of shape (n, k) and a
     dict of device timings. ``workspace`` (uint8 CUDA tensor of at least
-    :func:`workspace_bytes` bytes) is allocated here when not given.
+    :func:`workspace_bytes` (n, d, k) bytes) is allocated here when not given.
     """
     import torch
 
@@ -182,7 +182,7 @@ def brute_force_knn_device(x, k: int, distance=L2Squared(), out_ids=None, out_di
         out_ids = torch.empty((n, max(k, 0)), dtype=torch.int32, device=dev)
     if out_dists is None:
         out_dists = torch.empty((n, max(k, 0)), dtype=torch.float32, device=dev)
-    wsb = workspace_bytes(n, d)
+    wsb = workspace_bytes(n, d, k)
     if workspace is None:
         workspace = torch.empty(wsb, dtype=torch.uint8, device=dev)
     stats = KnngGpuStats()
@@ -218,12 +218,18 @@ def knn_u8(packed, norms, n: int, d: int, q_begin: int, q_count: int, k: int, di
     return stats.as_dict()
 
 
-def knn_f32(x, n: int, d: int, q_begin: int, q_count: int, k: int, distance, out_ids, out_dists,
+def knn_f32_scratch_bytes(n: int, d: int, q_count: int, k: int) -> int:
+    return int(gpu_lib().knng_gpu_knn_f32_scratch_bytes(n, d, q_count, k))
+
+
+def knn_f32(x, n: int, d: int, q_begin: int, q_count: int, k: int, distance, out_ids, out_dists, scratch,
             stream=None) -> dict:
-    """Exact fp32 KNN of rows [q_begin, q_begin+q_count) of x against all n rows."""
+    """KNN of fp32 rows [q_begin, q_begin+q_count) of x against all n rows
+    (tensor-core candidate filter, exact re-rank, exact fallback)."""
     stats = KnngGpuStats()
     check(gpu_lib().knng_gpu_knn_f32(_ptr(x), n, d, q_begin, q_count, k, _metric_id(distance), _ptr(out_ids),
-                                     _ptr(out_dists), _stream_handle(stream), ctypes.byref(stats)))
+                                     _ptr(out_dists), _ptr(scratch), scratch.numel(), _stream_handle(stream),
+                                     ctypes.byref(stats)))
     return stats.as_dict()
 
 

@@ -2,10 +2,12 @@
 // orchestration of the kernels: integer check + u8 pack + row norms, the
 // fused tensor-core KNN, and the exact fp32 kernel.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <climits>
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -14,7 +16,8 @@
 #include <string>
 
 #include "knn_exact.cuh"
-#include "knn_u8_tc.cuh"
+#include "knn_rerank.cuh"
+#include "knn_tc.cuh"
 #include "knng_gpu.h"
 
 using namespace knng_b200;
@@ -132,19 +135,19 @@ knng_gpu_status get_encode_fn(EncodeTiledFn* out)
     return KNNG_GPU_OK;
 }
 
-// rows x pitch u8, box 128 rows x 128 bytes, 128-byte swizzle; rows past the
-// end read as zeros.
-knng_gpu_status make_u8_map(CUtensorMap* map, const uint8_t* base, uint64_t rows, uint64_t pitch)
+// rows x pitch elements, box 128 rows x 128 bytes, 128-byte swizzle; rows
+// past the end read as zeros.
+knng_gpu_status make_map(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void* base,
+                         uint64_t rows, uint64_t pitch_elems)
 {
     EncodeTiledFn enc;
     KNNG_TRY(get_encode_fn(&enc));
-    const cuuint64_t dims[2] = {pitch, rows};
-    const cuuint64_t strides[1] = {pitch};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kChunkBytes), static_cast<cuuint32_t>(kTileRows)};
+    const cuuint64_t dims[2] = {pitch_elems, rows};
+    const cuuint64_t strides[1] = {pitch_elems * elem_bytes};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kChunkBytes / elem_bytes), static_cast<cuuint32_t>(kTileRows)};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return fail(KNNG_GPU_CUDA_ERROR, "knng::gpu: cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
     return KNNG_GPU_OK;
@@ -174,56 +177,55 @@ ScratchU8 carve_scratch_u8(void* p, uint64_t q_count)
     return s;
 }
 
-template <int MT, int BN, int NBUF, int SPLIT, int METRIC, class TopK>
-knng_gpu_status launch_u8_t(const CUtensorMap& mq, const CUtensorMap& mb, const KnnU8Params& p, cudaStream_t st)
+struct TcMaps {
+    CUtensorMap q0, q1, b0, b1;
+};
+
+template <class Elem, int MT, int NBUF, bool A_STREAM, int METRIC, class TopK>
+knng_gpu_status launch_tc_t(const TcMaps& m, const KnnTcParams& p, cudaStream_t st)
 {
-    const SmemLayoutU8 L = smem_layout_u8(MT, BN, p.kchunks, p.stages, SPLIT, SPLIT > 1 ? TopK::kRegs / 2 : 0);
+    const SmemLayoutTc L = smem_layout_tc(Elem::kPlanes, MT, A_STREAM, p.kchunks, p.stages);
     const uint32_t smem = L.total + 1024;
-    auto kern = knn_u8_tc_kernel<MT, BN, NBUF, SPLIT, METRIC, TopK>;
+    auto kern = knn_tc_kernel<Elem, MT, NBUF, A_STREAM, METRIC, TopK>;
     KNNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const uint32_t n_qtiles = (p.n_queries + MT * kTileRows - 1) / (MT * kTileRows);
     const uint32_t grid = std::min<uint32_t>(n_qtiles, static_cast<uint32_t>(sm_count()));
-    kern<<<grid, 64 + 128 * MT * SPLIT, smem, st>>>(mq, mb, p);
+    kern<<<grid, 64 + 128 * MT, smem, st>>>(m.q0, m.q1, m.b0, m.b1, p);
     KNNG_CUDA(cudaGetLastError());
     return KNNG_GPU_OK;
 }
 
-template <int MT, int BN, int NBUF, int METRIC>
-knng_gpu_status launch_u8_k(const CUtensorMap& mq, const CUtensorMap& mb, const KnnU8Params& p, int split,
-                            cudaStream_t st)
+// Stages that fit the shared-memory budget for a tile configuration.
+uint32_t pick_stages(int planes, int mt, bool a_stream, uint32_t kchunks)
 {
-    (void)split;  // the column-split epilogue (SPLIT = 2) is not instantiated
-    if (p.k <= 10) return launch_u8_t<MT, BN, NBUF, 1, METRIC, RegTopK<10>>(mq, mb, p, st);
-    if (p.k <= 16) return launch_u8_t<MT, BN, NBUF, 1, METRIC, RegTopK<16>>(mq, mb, p, st);
-    if (p.k <= 32) return launch_u8_t<MT, BN, NBUF, 1, METRIC, RegTopK<32>>(mq, mb, p, st);
+    const SmemLayoutTc L0 = smem_layout_tc(planes, mt, a_stream, kchunks, 0);
+    const uint32_t budget = 227u * 1024u - 1024u;
+    if (L0.total >= budget) return 0;
+    uint32_t s = std::min<uint32_t>(16, (budget - L0.total) / L0.stage_bytes);
+    if (const char* sv = std::getenv("KNNG_GPU_STAGES")) s = std::min<uint32_t>(s, std::atoi(sv));
+    return s;
+}
+
+template <int MT, int METRIC>
+knng_gpu_status launch_u8_k(const TcMaps& m, const KnnTcParams& p, cudaStream_t st)
+{
+    if (p.k <= 10) return launch_tc_t<ElemU8, MT, 2, false, METRIC, RegTopK<10>>(m, p, st);
+    if (p.k <= 16) return launch_tc_t<ElemU8, MT, 2, false, METRIC, RegTopK<16>>(m, p, st);
+    if (p.k <= 32) return launch_tc_t<ElemU8, MT, 2, false, METRIC, RegTopK<32>>(m, p, st);
     if constexpr (MT == 1) {
-        if (p.k <= 64) return launch_u8_t<MT, BN, NBUF, 1, METRIC, RegTopK<64>>(mq, mb, p, st);
+        if (p.k <= 64) return launch_tc_t<ElemU8, MT, 2, false, METRIC, RegTopK<64>>(m, p, st);
     }
-    if (p.k <= 128) return launch_u8_t<MT, BN, NBUF, 1, METRIC, HeapTopK<128>>(mq, mb, p, st);
-    return launch_u8_t<MT, BN, NBUF, 1, METRIC, HeapTopK<KNNG_GPU_MAX_K>>(mq, mb, p, st);
+    if (p.k <= 128) return launch_tc_t<ElemU8, MT, 2, false, METRIC, HeapTopK<128>>(m, p, st);
+    return launch_tc_t<ElemU8, MT, 2, false, METRIC, HeapTopK<KNNG_GPU_MAX_K>>(m, p, st);
 }
 
-// Tile shapes of the fused kernel: (query tiles per CTA, base rows per tile,
-// TMEM accumulator buffers).
-struct TileShape {
-    int mt, bn, nbuf, split;
-};
-
-template <int MT, int BN, int NBUF>
-knng_gpu_status launch_u8_m(const CUtensorMap& mq, const CUtensorMap& mb, const KnnU8Params& p, int metric,
-                            int split, cudaStream_t st)
+template <bool A_STREAM, int METRIC>
+knng_gpu_status launch_bf16_k(const TcMaps& m, const KnnTcParams& p, cudaStream_t st)
 {
-    return metric == 0 ? launch_u8_k<MT, BN, NBUF, 0>(mq, mb, p, split, st)
-                       : launch_u8_k<MT, BN, NBUF, 1>(mq, mb, p, split, st);
-}
-
-knng_gpu_status launch_u8(const CUtensorMap& mq, const CUtensorMap& mb, const KnnU8Params& p, TileShape ts,
-                          int metric, cudaStream_t st)
-{
-    // Measured alternatives (BN = 256 with one TMEM buffer, MT = 1 with four
-    // buffers, a two-way column split of the epilogue) were slower at d = 128.
-    if (ts.mt == 2) return launch_u8_m<2, 128, 2>(mq, mb, p, metric, 1, st);
-    return launch_u8_m<1, 128, 2>(mq, mb, p, metric, 1, st);
+    if (p.k <= 32) return launch_tc_t<ElemBf16x3, 1, 2, A_STREAM, METRIC, RegTopK<32>>(m, p, st);
+    if (p.k <= 64) return launch_tc_t<ElemBf16x3, 1, 2, A_STREAM, METRIC, RegTopK<64>>(m, p, st);
+    if (p.k <= 256) return launch_tc_t<ElemBf16x3, 1, 2, A_STREAM, METRIC, HeapTopK<256>>(m, p, st);
+    return launch_tc_t<ElemBf16x3, 1, 2, A_STREAM, METRIC, HeapTopK<KNNG_GPU_MAX_K + 64>>(m, p, st);
 }
 
 template <int METRIC, class TopK, class T>
@@ -289,6 +291,15 @@ struct EventTimer {
     }
 };
 
+knng_gpu_status read_counters(const uint32_t* d_counters, uint32_t* host, cudaStream_t st)
+{
+    KNNG_CUDA(cudaMemcpyAsync(host, d_counters, 8, cudaMemcpyDeviceToHost, st));
+    KNNG_CUDA(cudaStreamSynchronize(st));
+    if (host[1] != 0)
+        return fail(KNNG_GPU_TIMEOUT, "knng::gpu: a bounded device wait gave up (code " + std::to_string(host[1]) + ")");
+    return KNNG_GPU_OK;
+}
+
 knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_t n, uint64_t d, uint64_t q_begin,
                             uint64_t q_count, uint64_t k, int metric, uint32_t* ids, float* dists, void* scratch,
                             uint64_t scratch_bytes, cudaStream_t st, knng_gpu_stats* stats)
@@ -304,10 +315,10 @@ knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_
     EventTimer tk(stats != nullptr), tf(stats != nullptr);
     tk.start(st);
     if (d <= kMaxTensorDim) {
-        CUtensorMap mq, mb;
-        KNNG_TRY(make_u8_map(&mq, packed, n, pitch));
-        KNNG_TRY(make_u8_map(&mb, packed, n, pitch));
-        KnnU8Params p{};
+        TcMaps m;
+        KNNG_TRY(make_map(&m.q0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, packed, n, pitch));
+        m.q1 = m.b0 = m.b1 = m.q0;
+        KnnTcParams p{};
         p.base_norms = norms;
         p.query_norms = norms + q_begin;
         p.n_base = n;
@@ -325,15 +336,15 @@ knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_
         p.error = reinterpret_cast<int*>(sc.counters + 1);
         if (const char* dbg = std::getenv("KNNG_GPU_DEBUG_FLAGS")) p.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
         // Two query tiles per CTA need k <= 32 (register budget of 320 threads).
-        TileShape ts = (p.kchunks <= 2 && k <= 32) ? TileShape{2, 128, 2, 1} : TileShape{1, 128, 2, 1};
-        const uint32_t fixed = smem_layout_u8(ts.mt, ts.bn, p.kchunks, 0, ts.split, ts.split > 1 ? 16 : 0).total + 1024;
-        const uint32_t budget = 227u * 1024u;
-        const uint32_t stage_bytes = (ts.bn / kTileRows) * kBoxBytes;
-        p.stages = std::min<uint32_t>(16, (budget - fixed) / stage_bytes);
-        if (const char* sv = std::getenv("KNNG_GPU_STAGES")) p.stages = std::min<uint32_t>(p.stages, std::atoi(sv));
-        if (p.stages < 2 || (ts.mt > 1 && p.stages < p.kchunks))
+        const int mt = (p.kchunks <= 2 && k <= 32) ? 2 : 1;
+        p.stages = pick_stages(1, mt, false, p.kchunks);
+        if (p.stages < 2 || (mt > 1 && p.stages < p.kchunks))
             return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: shared memory budget exceeded");
-        knng_gpu_status s = launch_u8(mq, mb, p, ts, metric, st);
+        knng_gpu_status s;
+        if (mt == 2)
+            s = metric == 0 ? launch_u8_k<2, 0>(m, p, st) : launch_u8_k<2, 1>(m, p, st);
+        else
+            s = metric == 0 ? launch_u8_k<1, 0>(m, p, st) : launch_u8_k<1, 1>(m, p, st);
         KNNG_TRY(s);
         tk.stop(st);
         // Rows whose fp32 sums may round: recompute exactly (device-side
@@ -377,11 +388,7 @@ knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_
         tf.stop(st);
     }
     uint32_t host_counters[2] = {0, 0};
-    KNNG_CUDA(cudaMemcpyAsync(host_counters, sc.counters, 8, cudaMemcpyDeviceToHost, st));
-    KNNG_CUDA(cudaStreamSynchronize(st));
-    if (host_counters[1] != 0)
-        return fail(KNNG_GPU_TIMEOUT, "knng::gpu: a bounded device wait gave up (code " +
-                                          std::to_string(host_counters[1]) + ")");
+    KNNG_TRY(read_counters(sc.counters, host_counters, st));
     if (stats) {
         stats->path = KNNG_PATH_U8_TENSOR;
         stats->fallback_rows = host_counters[0];
@@ -392,12 +399,170 @@ knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_
     return KNNG_GPU_OK;
 }
 
+// ------------------------------------------------------------------ fp32 path
+// Candidates kept per row by the bf16x3 filter: k plus a margin, at most n - 1.
+uint64_t f32_candidates(uint64_t n, uint64_t k) { return std::min<uint64_t>(n - 1, k + 32); }
+
+uint64_t f32_pitch_elems(uint64_t d) { return align_up(d, kChunkBytes / 2); }
+
+struct ScratchF32 {
+    double* sums;
+    float* mu;
+    unsigned int* max_norm_bits;
+    __nv_bfloat16* hi;
+    __nv_bfloat16* lo;
+    float* norms;
+    uint32_t* cand_ids;
+    int32_t* cand_keys;
+    uint32_t* fallback_rows;
+    uint32_t* counters;  // [0] fallback count, [1] error flag, [2] observed error ratio (fp32 bits)
+    uint64_t total;
+};
+
+ScratchF32 layout_scratch_f32(void* base, uint64_t n, uint64_t d, uint64_t q_count, uint64_t k)
+{
+    ScratchF32 s{};
+    uint8_t* p = static_cast<uint8_t*>(base);
+    uint64_t off = 0;
+    auto take = [&](uint64_t bytes) {
+        uint8_t* r = p ? p + off : nullptr;
+        off = align_up(off + bytes, 256);
+        return r;
+    };
+    const uint64_t pitch = f32_pitch_elems(d);
+    const uint64_t c = f32_candidates(n, k);
+    s.sums = reinterpret_cast<double*>(take(d * 8));
+    s.mu = reinterpret_cast<float*>(take(d * 4));
+    s.max_norm_bits = reinterpret_cast<unsigned int*>(take(4));
+    s.hi = reinterpret_cast<__nv_bfloat16*>(take(n * pitch * 2));
+    s.lo = reinterpret_cast<__nv_bfloat16*>(take(n * pitch * 2));
+    s.norms = reinterpret_cast<float*>(take(n * 4));
+    s.cand_ids = reinterpret_cast<uint32_t*>(take(q_count * c * 4));
+    s.cand_keys = reinterpret_cast<int32_t*>(take(q_count * c * 4));
+    s.fallback_rows = reinterpret_cast<uint32_t*>(take(q_count * 4));
+    s.counters = reinterpret_cast<uint32_t*>(take(16));
+    s.total = off;
+    return s;
+}
+
+// eps coefficient of the re-rank proof (knn_rerank.cuh).
+double f32_gamma(uint64_t d, int metric)
+{
+    const double dd = static_cast<double>(d);
+    const double split = std::ldexp(1.0, -14), acc = (3.0 * dd / 16.0 + 3.0) * std::ldexp(1.0, -22);
+    const double ref = (dd + 3.0) * std::ldexp(1.0, -24);
+    double g = metric == 0 ? 2.0 * (split + acc) + std::ldexp(1.0, -19) + ref : split + acc + std::ldexp(1.0, -21) + ref;
+    if (const char* gs = std::getenv("KNNG_GPU_GAMMA_SCALE")) g *= std::atof(gs);  // experiments only
+    return g;
+}
+
 knng_gpu_status knn_f32_impl(const float* x, uint64_t n, uint64_t d, uint64_t q_begin, uint64_t q_count, uint64_t k,
-                             int metric, uint32_t* ids, float* dists, cudaStream_t st, knng_gpu_stats* stats)
+                             int metric, uint32_t* ids, float* dists, void* scratch, uint64_t scratch_bytes,
+                             cudaStream_t st, knng_gpu_stats* stats)
 {
     if (q_begin + q_count > n) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: query range exceeds the base");
-    EventTimer tk(stats != nullptr);
+    const ScratchF32 sc = layout_scratch_f32(scratch, n, d, q_count, k);
+    if (scratch_bytes < sc.total || (reinterpret_cast<uintptr_t>(scratch) & 255))
+        return fail(KNNG_GPU_WORKSPACE_TOO_SMALL, "knng::gpu: fp32 scratch smaller than knng_gpu_knn_f32_scratch_bytes");
+    if (q_count == 0) return KNNG_GPU_OK;
+    const uint64_t pitch = f32_pitch_elems(d);
+    const uint64_t c = f32_candidates(n, k);
+    const uint32_t kchunks = static_cast<uint32_t>(pitch * 2 / kChunkBytes);
+    EventTimer tk(stats != nullptr), tf(stats != nullptr);
     tk.start(st);
+    KNNG_CUDA(cudaMemsetAsync(sc.counters, 0, 16, st));
+    KNNG_CUDA(cudaMemsetAsync(sc.max_norm_bits, 0, 4, st));
+    uint32_t launches = 0;
+    if (metric == 0) {
+        // L2 is translation invariant: centre the rows to shrink the error bound.
+        KNNG_CUDA(cudaMemsetAsync(sc.sums, 0, d * 8, st));
+        column_sum_kernel<<<static_cast<uint32_t>((n + 255) / 256), 256, 0, st>>>(x, n, static_cast<uint32_t>(d),
+                                                                                 sc.sums);
+        column_mean_kernel<<<static_cast<uint32_t>((d + 255) / 256), 256, 0, st>>>(sc.sums, n, static_cast<uint32_t>(d),
+                                                                                  sc.mu);
+        launches += 2;
+    }
+    {
+        const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((n + 7) / 8, 148ull * 16));
+        split_bf16_kernel<<<blocks, 256, 0, st>>>(x, n, static_cast<uint32_t>(d), static_cast<uint32_t>(pitch),
+                                                  metric == 0 ? sc.mu : nullptr, sc.hi, sc.lo, sc.norms,
+                                                  sc.max_norm_bits);
+        KNNG_CUDA(cudaGetLastError());
+        launches += 1;
+    }
+    // Candidate filter on the tensor cores.
+    TcMaps m;
+    KNNG_TRY(make_map(&m.b0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sc.hi, n, pitch));
+    KNNG_TRY(make_map(&m.b1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sc.lo, n, pitch));
+    m.q0 = m.b0;
+    m.q1 = m.b1;
+    KnnTcParams p{};
+    p.base_norms = sc.norms;
+    p.n_base = n;
+    p.base_id0 = 0;
+    p.n_queries = static_cast<uint32_t>(q_count);
+    p.query_row0 = static_cast<uint32_t>(q_begin);
+    p.query_id0 = static_cast<uint32_t>(q_begin);
+    p.exclude_self = 1;
+    p.k = static_cast<uint32_t>(c);
+    p.kchunks = kchunks;
+    p.out_ids = sc.cand_ids;
+    p.out_keys = sc.cand_keys;
+    p.error = reinterpret_cast<int*>(sc.counters + 1);
+    if (const char* dbg = std::getenv("KNNG_GPU_DEBUG_FLAGS")) p.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
+    bool a_stream = false;
+    p.stages = pick_stages(2, 1, false, kchunks);
+    if (p.stages < 2) {
+        a_stream = true;
+        p.stages = pick_stages(2, 1, true, kchunks);
+    }
+    if (p.stages < 2) return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: shared memory budget exceeded");
+    knng_gpu_status s;
+    if (a_stream)
+        s = metric == 0 ? launch_bf16_k<true, 0>(m, p, st) : launch_bf16_k<true, 1>(m, p, st);
+    else
+        s = metric == 0 ? launch_bf16_k<false, 0>(m, p, st) : launch_bf16_k<false, 1>(m, p, st);
+    KNNG_TRY(s);
+    // Exact re-rank of the candidates with the proof of exactness.
+    RerankParams r{};
+    r.x = x;
+    r.d = d;
+    r.n = n;
+    r.q_begin = static_cast<uint32_t>(q_begin);
+    r.n_queries = static_cast<uint32_t>(q_count);
+    r.c = static_cast<uint32_t>(c);
+    r.k = static_cast<uint32_t>(k);
+    r.cand_ids = sc.cand_ids;
+    r.cand_keys = sc.cand_keys;
+    r.norms = sc.norms;
+    r.max_norm_bits = sc.max_norm_bits;
+    r.gamma = f32_gamma(d, metric);
+    r.out_ids = ids;
+    r.out_dists = dists;
+    r.fallback_rows = sc.fallback_rows;
+    r.fallback_count = sc.counters;
+    r.err_ratio_bits = sc.counters + 2;
+    {
+        const uint32_t warps = 32 * kRerankWarps;
+        const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((q_count + kRerankWarps - 1) / kRerankWarps,
+                                                                         148ull * 8));
+        const uint32_t cpl = static_cast<uint32_t>((c + 31) / 32);
+        (void)warps;
+        if (cpl <= 2)
+            metric == 0 ? rerank_kernel<0, 2><<<blocks, 32 * kRerankWarps, 0, st>>>(r)
+                        : rerank_kernel<1, 2><<<blocks, 32 * kRerankWarps, 0, st>>>(r);
+        else if (cpl <= 8)
+            metric == 0 ? rerank_kernel<0, 8><<<blocks, 32 * kRerankWarps, 0, st>>>(r)
+                        : rerank_kernel<1, 8><<<blocks, 32 * kRerankWarps, 0, st>>>(r);
+        else
+            metric == 0 ? rerank_kernel<0, 34><<<blocks, 32 * kRerankWarps, 0, st>>>(r)
+                        : rerank_kernel<1, 34><<<blocks, 32 * kRerankWarps, 0, st>>>(r);
+        KNNG_CUDA(cudaGetLastError());
+        launches += 2;
+    }
+    tk.stop(st);
+    // Rows the proof could not certify: exact kernel on the original rows.
+    tf.start(st);
     KnnExactParams<float> e{};
     e.base = x;
     e.base_stride = d;
@@ -409,14 +574,26 @@ knng_gpu_status knn_f32_impl(const float* x, uint64_t n, uint64_t d, uint64_t q_
     e.exclude_self = 1;
     e.d = static_cast<uint32_t>(d);
     e.k = static_cast<uint32_t>(k);
+    e.row_list = sc.fallback_rows;
+    e.row_count = sc.counters;
     e.out_ids = ids;
     e.out_dists = dists;
     KNNG_TRY(launch_exact(e, metric, static_cast<uint32_t>(q_count), st));
-    tk.stop(st);
+    tf.stop(st);
+    launches += 1;
+    uint32_t host_counters[2] = {0, 0};
+    KNNG_TRY(read_counters(sc.counters, host_counters, st));
+    uint32_t ratio_bits = 0;
+    KNNG_CUDA(cudaMemcpy(&ratio_bits, sc.counters + 2, 4, cudaMemcpyDeviceToHost));
     if (stats) {
-        stats->path = KNNG_PATH_F32_EXACT;
+        float ratio;
+        std::memcpy(&ratio, &ratio_bits, 4);
+        stats->f32_err_ratio = ratio;
+        stats->path = KNNG_PATH_F32_TENSOR;
+        stats->fallback_rows = host_counters[0];
         stats->knn_ms = tk.ms();
-        stats->kernel_launches += 1;
+        stats->fallback_ms = tf.ms();
+        stats->kernel_launches += launches;
     }
     return KNNG_GPU_OK;
 }
@@ -425,7 +602,8 @@ struct WorkspaceLayout {
     uint64_t packed, norms, flag, scratch, total;
 };
 
-WorkspaceLayout workspace_layout(uint64_t n, uint64_t d)
+// The u8 path and the fp32 path share one workspace (only one of them runs).
+WorkspaceLayout workspace_layout(uint64_t n, uint64_t d, uint64_t k)
 {
     WorkspaceLayout w;
     const uint64_t pitch = knng_gpu_padded_dim(d);
@@ -433,7 +611,9 @@ WorkspaceLayout workspace_layout(uint64_t n, uint64_t d)
     w.norms = align_up(w.packed + n * pitch, 256);
     w.flag = align_up(w.norms + n * 4, 256);
     w.scratch = w.flag + 256;
-    w.total = w.scratch + scratch_u8_bytes(n);
+    const uint64_t u8_total = w.scratch + scratch_u8_bytes(n);
+    const uint64_t f32_total = w.scratch + layout_scratch_f32(nullptr, n, d, n, k).total;
+    w.total = std::max(u8_total, f32_total);
     return w;
 }
 
@@ -454,7 +634,7 @@ knng_gpu_status device_pipeline(const float* x, uint64_t n, uint64_t d, uint64_t
                                 float* dists, void* ws, uint64_t ws_bytes, cudaStream_t st, knng_gpu_stats* stats)
 {
     KNNG_TRY(validate(n, d, k, metric));
-    const WorkspaceLayout w = workspace_layout(n, d);
+    const WorkspaceLayout w = workspace_layout(n, d, k);
     if (ws_bytes < w.total || (reinterpret_cast<uintptr_t>(ws) & 255))
         return fail(KNNG_GPU_WORKSPACE_TOO_SMALL, "knng::gpu: workspace smaller than knng_gpu_workspace_bytes or "
                                                   "not 256-byte aligned");
@@ -479,7 +659,9 @@ knng_gpu_status device_pipeline(const float* x, uint64_t n, uint64_t d, uint64_t
         KNNG_TRY(knn_u8_impl(packed, norms, n, d, 0, n, k, metric, ids, dists, base + w.scratch, w.total - w.scratch,
                              st, stats));
     } else {
-        KNNG_TRY(knn_f32_impl(x, n, d, 0, n, k, metric, ids, dists, st, stats));
+        // The packed bytes are meaningless for such data; the fp32 path
+        // reuses the whole workspace.
+        KNNG_TRY(knn_f32_impl(x, n, d, 0, n, k, metric, ids, dists, base, w.total, st, stats));
     }
     tall.stop(st);
     if (stats) {
@@ -563,7 +745,12 @@ int knng_gpu_device_count(void)
 
 uint64_t knng_gpu_padded_dim(uint64_t d) { return align_up(d == 0 ? 1 : d, kChunkBytes); }
 
-uint64_t knng_gpu_workspace_bytes(uint64_t n, uint64_t d) { return workspace_layout(n, d).total; }
+uint64_t knng_gpu_workspace_bytes(uint64_t n, uint64_t d, uint64_t k) { return workspace_layout(n, d, k).total; }
+
+uint64_t knng_gpu_knn_f32_scratch_bytes(uint64_t n, uint64_t d, uint64_t q_count, uint64_t k)
+{
+    return layout_scratch_f32(nullptr, n, d, q_count, k).total;
+}
 
 uint64_t knng_gpu_knn_scratch_bytes(uint64_t q_count) { return scratch_u8_bytes(q_count); }
 
@@ -587,13 +774,13 @@ knng_gpu_status knng_gpu_knn_u8(const uint8_t* d_packed, const int32_t* d_norms,
 }
 
 knng_gpu_status knng_gpu_knn_f32(const float* d_x, uint64_t n, uint64_t d, uint64_t q_begin, uint64_t q_count,
-                                 uint64_t k, int metric, uint32_t* d_ids, float* d_dists, void* stream,
-                                 knng_gpu_stats* stats)
+                                 uint64_t k, int metric, uint32_t* d_ids, float* d_dists, void* d_scratch,
+                                 uint64_t scratch_bytes, void* stream, knng_gpu_stats* stats)
 {
     g_last_error.clear();
     KNNG_TRY(validate(n, d, k, metric));
-    return knn_f32_impl(d_x, n, d, q_begin, q_count, k, metric, d_ids, d_dists, static_cast<cudaStream_t>(stream),
-                        stats);
+    return knn_f32_impl(d_x, n, d, q_begin, q_count, k, metric, d_ids, d_dists, d_scratch, scratch_bytes,
+                        static_cast<cudaStream_t>(stream), stats);
 }
 
 knng_gpu_status knng_gpu_brute_force_device(const float* d_data, uint64_t n, uint64_t d, uint64_t k, int metric,
@@ -623,7 +810,7 @@ knng_gpu_status knng_gpu_brute_force(const float* data, uint64_t n, uint64_t d, 
     c.device = dev;
     if (!c.stream) KNNG_CUDA(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
     cudaStream_t st = c.stream;
-    const uint64_t ws_bytes = knng_gpu_workspace_bytes(n, d);
+    const uint64_t ws_bytes = knng_gpu_workspace_bytes(n, d, k);
     KNNG_TRY(grow(&c.x, &c.x_cap, n * d * sizeof(float)));
     KNNG_TRY(grow(&c.ids, &c.ids_cap, n * k * sizeof(uint32_t)));
     KNNG_TRY(grow(&c.dists, &c.dists_cap, n * k * sizeof(float)));

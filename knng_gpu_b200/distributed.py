@@ -91,6 +91,7 @@ class ShardedBuilder:
         self.all_ids = torch.empty((self.world * self.max_shard, k), dtype=torch.int32, device=dev)
         self.all_dists = torch.empty((self.world * self.max_shard, k), dtype=torch.float32, device=dev)
         self.f32_full = None
+        self.f32_scratch = None
         self.last_stats: dict = {}
 
     @property
@@ -127,8 +128,11 @@ class ShardedBuilder:
                 dist.all_gather_into_tensor(self.f32_full,
                                             self.f32_full[self.rank * self.s:(self.rank + 1) * self.s],
                                             group=self.group)
+            if self.f32_scratch is None:
+                nb = api.knn_f32_scratch_bytes(self.n, self.d, self.max_shard, self.k)
+                self.f32_scratch = torch.empty(nb, dtype=torch.uint8, device=self.dev)
             self.last_stats = api.knn_f32(self.f32_full, self.n, self.d, sh.start, sh.count, self.k, self.metric,
-                                          ids, dists)
+                                          ids, dists, self.f32_scratch)
         if self.world == 1:
             return ids, dists
         dist.all_gather_into_tensor(self.all_ids, self.ids, group=self.group)

@@ -35,7 +35,8 @@ def test_library_exports_every_declared_symbol():
 def test_padded_dim_and_workspace():
     assert padded_dim(1) == 128 and padded_dim(128) == 128 and padded_dim(129) == 256
     assert padded_dim(960) == 1024 and padded_dim(784) == 896
-    assert workspace_bytes(1000, 128) >= 1000 * 128 + 1000 * 4
+    assert workspace_bytes(1000, 128, 10) >= 1000 * 128 + 1000 * 4
+    assert workspace_bytes(1000, 960, 100) >= 2 * 1000 * 1024 * 2  # fp32 path: bf16 hi + lo planes
 
 
 @pytest.mark.parametrize(

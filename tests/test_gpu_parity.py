@@ -64,8 +64,14 @@ def test_gpu_matches_reference_golden(cuda_ok, case):
 def test_path_selection(cuda_ok):
     _, _, s = run_gpu(BY_NAME["cfg1_u8_n2000_d128_k10_l2"].make(), 10, 0)
     assert s["path"] == 0 and s["fallback_rows"] == 0
-    _, _, s = run_gpu(BY_NAME["cfg2_gmm_n2000_d128_k32_l2"].make(), 32, 0)
-    assert s["path"] == 1
+    # non-integer data: bf16x3 tensor-core filter + exact re-rank; the error
+    # bound must certify almost every row without the exact fallback
+    for name, k, metric in [("cfg2_gmm_n2000_d128_k32_l2", 32, 0), ("cfg4_unit_n800_d960_k100_l2", 100, 0),
+                            ("pm1_n1024_d128_k10_l2", 10, 0), ("pm1_n500_d64_k10_negip", 10, 1)]:
+        x = BY_NAME[name].make()
+        _, _, s = run_gpu(x, k, metric)
+        assert s["path"] == 1
+        assert s["fallback_rows"] <= 0.05 * x.shape[0], (name, s)
     # {0,255} rows at d=1024: L2 distances exceed 2^24, so rows go to the exact kernel
     _, _, s = run_gpu(BY_NAME["bimodal_n500_d1024_k5_l2"].make(), 5, 0)
     assert s["path"] == 0 and s["fallback_rows"] > 0
@@ -90,6 +96,18 @@ def test_ragged_sizes_against_oracle(cuda_ok):
             oi, od = oracle_knn(x, k, 0)
             assert np.array_equal(ids, oi), (n, k)
             assert np.array_equal(dists, od), (n, k)
+
+
+def test_fp32_path_larger_against_oracle(cuda_ok):
+    """fp32 rows through the tensor-core filter at a size with many tiles."""
+    for kind, n, d, k, metric in [(syn.KIND_GAUSSIAN_MIXTURE, 6000, 128, 32, 0), (syn.KIND_UNIFORM_PM1, 3000, 200, 16, 1),
+                                  (syn.KIND_UNIT_ROWS, 2500, 960, 100, 0)]:
+        x = syn.generate(kind, 11, n, d, components=50, sigma=0.1)
+        ids, dists, s = run_gpu(x, k, metric)
+        oi, od = oracle_knn(x, k, metric)
+        assert s["path"] == 1
+        assert np.array_equal(ids, oi), (kind, np.sum(np.any(ids != oi, axis=1)))
+        assert np.array_equal(dists.view(np.uint32), od.view(np.uint32))
 
 
 def test_device_api_and_determinism(cuda_ok):
