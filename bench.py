@@ -154,7 +154,7 @@ class ClockSampler:
                  "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
         return self
@@ -218,13 +218,12 @@ def main() -> None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    # ---- device-resident steps
-    for _ in range(args.warmup):
-        builder.build(x_slice)
-    barrier()
+    # ---- device-resident steps (clock sampling spans warm-up and timed steps)
     knn_ms = []
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        for _ in range(args.warmup):
+            builder.build(x_slice)
         barrier()
         ev0.record(stream)
         for _ in range(args.steps):
@@ -233,6 +232,11 @@ def main() -> None:
         ev1.record(stream)
         barrier()
     step_ms = ev0.elapsed_time(ev1) / args.steps
+    # one extra, separately timed build: where the time of a step goes
+    builder.timing = True
+    builder.build(x_slice)
+    phases = builder.phase_ms()
+    builder.timing = False
     launches_per_step = int(builder.last_stats.get("kernel_launches", 0)) + 1  # + pack
     t = torch.tensor([step_ms], device=dev)
     if world > 1:
@@ -339,6 +343,7 @@ def main() -> None:
             "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clk.summary(),
             "gpu_launches": launches_per_step * args.steps, "parity_spot_check": recall_info,
             "path": builder.last_stats.get("path"), "fallback_rows": builder.last_stats.get("fallback_rows"),
+            "phase_ms_rank0": phases,
         }
         print(json.dumps(line))
     if world > 1:

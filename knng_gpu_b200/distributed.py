@@ -92,6 +92,10 @@ class ShardedBuilder:
         self.all_dists = torch.empty((self.world * self.max_shard, k), dtype=torch.float32, device=dev)
         self.f32_full = None
         self.f32_scratch = None
+        # Optional per-phase device timing (set .timing = True): CUDA events on
+        # the current stream; phase_ms() reads them after a build.
+        self.timing = False
+        self._marks: list = []
         self.last_stats: dict = {}
 
     @property
@@ -104,16 +108,21 @@ class ShardedBuilder:
         Returns (ids, dists) of shape (n, k) on every rank (valid on all)."""
         lo, hi = self.slice_bounds
         assert x_slice.shape == (hi - lo, self.d)
+        self._marks = []
+        self._mark("start")
         self.flag.zero_()
         api.pack_u8(x_slice, self.packed[lo:hi], self.norms[lo:hi], self.flag)
+        self._mark("pack")
         if self.world > 1:
             dist.all_reduce(self.flag, op=dist.ReduceOp.MAX, group=self.group)
             dist.all_gather_into_tensor(self.packed, self.packed[self.rank * self.s:(self.rank + 1) * self.s],
                                         group=self.group)
             dist.all_gather_into_tensor(self.norms, self.norms[self.rank * self.s:(self.rank + 1) * self.s],
                                         group=self.group)
+        self._mark("exchange_base")
         # The flag decides the kernel family: one host read per build.
         integer = int(self.flag.item()) == 0
+        self._mark("flag_read")
         sh = self.shard
         ids = self.ids[: sh.count]
         dists = self.dists[: sh.count]
@@ -133,11 +142,25 @@ class ShardedBuilder:
                 self.f32_scratch = torch.empty(nb, dtype=torch.uint8, device=self.dev)
             self.last_stats = api.knn_f32(self.f32_full, self.n, self.d, sh.start, sh.count, self.k, self.metric,
                                           ids, dists, self.f32_scratch)
+        self._mark("knn")
         if self.world == 1:
             return ids, dists
         dist.all_gather_into_tensor(self.all_ids, self.ids, group=self.group)
         dist.all_gather_into_tensor(self.all_dists, self.dists, group=self.group)
-        return self._unpad(self.all_ids), self._unpad(self.all_dists)
+        out = self._unpad(self.all_ids), self._unpad(self.all_dists)
+        self._mark("gather_rows")
+        return out
+
+    def _mark(self, name: str) -> None:
+        if self.timing:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self._marks.append((name, ev))
+
+    def phase_ms(self) -> dict:
+        """Device time of each phase of the last build (needs .timing)."""
+        torch.cuda.synchronize()
+        return {b[0]: a[1].elapsed_time(b[1]) for a, b in zip(self._marks, self._marks[1:])}
 
     def _unpad(self, t: torch.Tensor) -> torch.Tensor:
         return unpad_shards(t, self.n, self.world)
