@@ -120,6 +120,23 @@ knng_gpu_status knng_gpu_knn_u8(const uint8_t* d_packed, const int32_t* d_norms,
                                 uint64_t q_begin, uint64_t q_count, uint64_t k, int metric, uint32_t* d_ids,
                                 float* d_dists, void* d_scratch, uint64_t scratch_bytes, void* stream,
                                 knng_gpu_stats* stats);
+/* knng_gpu_knn_u8_sets: query rows and base rows as separate packed sets
+ *   (cross-set KNN and the base blocks of a ring pass). Ids are global: base
+ *   row r is b_id0 + r, query row i is q_id0 + i; with exclude_self a query
+ *   never returns its own id (src/dist/brute_force_mpi.cpp:80-82 excludes by
+ *   global index the same way). Needs n_b >= k (+1 with exclude_self).
+ *   d_scratch: >= knng_gpu_knn_scratch_bytes(n_q) bytes.
+ * knng_gpu_merge_topk: row-wise merge of two sorted k-lists into the k best
+ *   by (distance, id), the TopK order (include/knng/top_k.hpp:56-72); merges
+ *   the per-block results of a ring pass. */
+knng_gpu_status knng_gpu_knn_u8_sets(const uint8_t* d_q_packed, const int32_t* d_q_norms, uint64_t n_q,
+                                     uint64_t q_id0, const uint8_t* d_b_packed, const int32_t* d_b_norms, uint64_t n_b,
+                                     uint64_t b_id0, uint64_t d, uint64_t k, int metric, int exclude_self,
+                                     uint32_t* d_ids, float* d_dists, void* d_scratch, uint64_t scratch_bytes,
+                                     void* stream, knng_gpu_stats* stats);
+knng_gpu_status knng_gpu_merge_topk(const uint32_t* d_a_ids, const float* d_a_dists, const uint32_t* d_b_ids,
+                                    const float* d_b_dists, uint64_t rows, uint64_t k, uint32_t* d_out_ids,
+                                    float* d_out_dists, void* stream);
 uint64_t knng_gpu_knn_f32_scratch_bytes(uint64_t n, uint64_t d, uint64_t q_count, uint64_t k);
 knng_gpu_status knng_gpu_knn_f32(const float* d_x, uint64_t n, uint64_t d, uint64_t q_begin, uint64_t q_count,
                                  uint64_t k, int metric, uint32_t* d_ids, float* d_dists, void* d_scratch,

@@ -18,6 +18,8 @@ from .api import (  # noqa: F401
     knn_f32_scratch_bytes,
     knn_scratch_bytes,
     knn_u8,
+    knn_u8_sets,
+    merge_topk,
     pack_u8,
     padded_dim,
     workspace_bytes,

@@ -27,6 +27,8 @@ GPU_SYMBOLS = (
     "knng_gpu_pack_u8",
     "knng_gpu_knn_scratch_bytes",
     "knng_gpu_knn_u8",
+    "knng_gpu_knn_u8_sets",
+    "knng_gpu_merge_topk",
     "knng_gpu_knn_f32_scratch_bytes",
     "knng_gpu_knn_f32",
     "knng_gpu_knn_u8_noalloc",
@@ -87,6 +89,13 @@ def gpu_lib() -> ctypes.CDLL:
                 [c_void_p, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_int, c_void_p, c_void_p,
                  c_void_p, c_uint64, c_void_p, st],
             ),
+            "knng_gpu_knn_u8_sets": (
+                c_int,
+                [c_void_p, c_void_p, c_uint64, c_uint64, c_void_p, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64,
+                 c_int, c_int, c_void_p, c_void_p, c_void_p, c_uint64, c_void_p, st],
+            ),
+            "knng_gpu_merge_topk": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_uint64, c_uint64, c_void_p,
+                                            c_void_p, c_void_p]),
             "knng_gpu_knn_u8_noalloc": (
                 c_int,
                 [c_void_p, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_int, c_void_p, c_void_p,

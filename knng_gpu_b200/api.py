@@ -218,6 +218,24 @@ def knn_u8(packed, norms, n: int, d: int, q_begin: int, q_count: int, k: int, di
     return stats.as_dict()
 
 
+def knn_u8_sets(q_packed, q_norms, q_id0: int, b_packed, b_norms, b_id0: int, d: int, k: int, distance,
+                exclude_self: bool, out_ids, out_dists, scratch, stream=None) -> dict:
+    """Fused KNN of packed query rows against a separate packed base (global ids)."""
+    stats = KnngGpuStats()
+    check(gpu_lib().knng_gpu_knn_u8_sets(_ptr(q_packed), _ptr(q_norms), q_packed.shape[0], q_id0, _ptr(b_packed),
+                                         _ptr(b_norms), b_packed.shape[0], b_id0, d, k, _metric_id(distance),
+                                         int(exclude_self), _ptr(out_ids), _ptr(out_dists), _ptr(scratch),
+                                         scratch.numel(), _stream_handle(stream), ctypes.byref(stats)))
+    return stats.as_dict()
+
+
+def merge_topk(a_ids, a_dists, b_ids, b_dists, out_ids, out_dists, stream=None) -> None:
+    """Row-wise merge of two sorted (rows, k) lists into the k best by (distance, id)."""
+    rows, k = a_ids.shape
+    check(gpu_lib().knng_gpu_merge_topk(_ptr(a_ids), _ptr(a_dists), _ptr(b_ids), _ptr(b_dists), rows, k,
+                                        _ptr(out_ids), _ptr(out_dists), _stream_handle(stream)))
+
+
 def knn_f32_scratch_bytes(n: int, d: int, q_count: int, k: int) -> int:
     return int(gpu_lib().knng_gpu_knn_f32_scratch_bytes(n, d, q_count, k))
 

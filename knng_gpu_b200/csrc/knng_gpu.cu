@@ -300,33 +300,65 @@ knng_gpu_status read_counters(const uint32_t* d_counters, uint32_t* host, cudaSt
     return KNNG_GPU_OK;
 }
 
-knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_t n, uint64_t d, uint64_t q_begin,
-                            uint64_t q_count, uint64_t k, int metric, uint32_t* ids, float* dists, void* scratch,
-                            uint64_t scratch_bytes, cudaStream_t st, knng_gpu_stats* stats)
+// Query rows and base rows as separate packed sets (they may be the same
+// buffer). Ids are global: base row r is id b_id0 + r, query row i is
+// q_id0 + i, and with exclude_self a query never returns its own id.
+struct U8Sets {
+    const uint8_t* q_packed;
+    const int32_t* q_norms;
+    uint64_t n_q;
+    uint64_t q_id0;
+    const uint8_t* b_packed;
+    const int32_t* b_norms;
+    uint64_t n_b;
+    uint64_t b_id0;
+    int exclude_self;
+};
+
+knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int metric, uint32_t* ids, float* dists,
+                                 void* scratch, uint64_t scratch_bytes, cudaStream_t st, knng_gpu_stats* stats)
 {
-    if (q_begin + q_count > n) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: query range exceeds the base");
+    const uint64_t q_count = z.n_q;
     if (scratch_bytes < scratch_u8_bytes(q_count))
         return fail(KNNG_GPU_WORKSPACE_TOO_SMALL, "knng::gpu: scratch smaller than knng_gpu_knn_scratch_bytes");
     if (q_count == 0) return KNNG_GPU_OK;
+    if (z.n_b < k + (z.exclude_self ? 1 : 0))
+        return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: fewer base rows than k");
     const uint64_t pitch = knng_gpu_padded_dim(d);
     ScratchU8 sc = carve_scratch_u8(scratch, q_count);
     KNNG_CUDA(cudaMemsetAsync(sc.counters, 0, 8, st));
     uint32_t launches = 1;
     EventTimer tk(stats != nullptr), tf(stats != nullptr);
     tk.start(st);
+    KnnExactParams<uint8_t> e{};
+    e.base = z.b_packed;
+    e.base_stride = pitch;
+    e.n_base = z.n_b;
+    e.base_id0 = static_cast<uint32_t>(z.b_id0);
+    e.queries = z.q_packed;
+    e.query_stride = pitch;
+    e.n_queries = static_cast<uint32_t>(q_count);
+    e.query_id0 = static_cast<uint32_t>(z.q_id0);
+    e.exclude_self = z.exclude_self;
+    e.d = static_cast<uint32_t>(d);
+    e.k = static_cast<uint32_t>(k);
+    e.out_ids = ids;
+    e.out_dists = dists;
     if (d <= kMaxTensorDim) {
         TcMaps m;
-        KNNG_TRY(make_map(&m.q0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, packed, n, pitch));
-        m.q1 = m.b0 = m.b1 = m.q0;
+        KNNG_TRY(make_map(&m.q0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.q_packed, q_count, pitch));
+        KNNG_TRY(make_map(&m.b0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.b_packed, z.n_b, pitch));
+        m.q1 = m.q0;
+        m.b1 = m.b0;
         KnnTcParams p{};
-        p.base_norms = norms;
-        p.query_norms = norms + q_begin;
-        p.n_base = n;
-        p.base_id0 = 0;
+        p.base_norms = z.b_norms;
+        p.query_norms = z.q_norms;
+        p.n_base = z.n_b;
+        p.base_id0 = static_cast<uint32_t>(z.b_id0);
         p.n_queries = static_cast<uint32_t>(q_count);
-        p.query_row0 = static_cast<uint32_t>(q_begin);
-        p.query_id0 = static_cast<uint32_t>(q_begin);
-        p.exclude_self = 1;
+        p.query_row0 = 0;
+        p.query_id0 = static_cast<uint32_t>(z.q_id0);
+        p.exclude_self = z.exclude_self;
         p.k = static_cast<uint32_t>(k);
         p.kchunks = static_cast<uint32_t>(pitch / kChunkBytes);
         p.out_ids = ids;
@@ -350,38 +382,12 @@ knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_
         // Rows whose fp32 sums may round: recompute exactly (device-side
         // count; CTAs past it exit at once).
         tf.start(st);
-        KnnExactParams<uint8_t> e{};
-        e.base = packed;
-        e.base_stride = pitch;
-        e.n_base = n;
-        e.queries = packed + q_begin * pitch;
-        e.query_stride = pitch;
-        e.n_queries = static_cast<uint32_t>(q_count);
-        e.query_id0 = static_cast<uint32_t>(q_begin);
-        e.exclude_self = 1;
-        e.d = static_cast<uint32_t>(d);
-        e.k = static_cast<uint32_t>(k);
         e.row_list = sc.fallback_rows;
         e.row_count = sc.counters;
-        e.out_ids = ids;
-        e.out_dists = dists;
         KNNG_TRY(launch_exact(e, metric, static_cast<uint32_t>(q_count), st));
         tf.stop(st);
         launches = 2;
     } else {
-        KnnExactParams<uint8_t> e{};
-        e.base = packed;
-        e.base_stride = pitch;
-        e.n_base = n;
-        e.queries = packed + q_begin * pitch;
-        e.query_stride = pitch;
-        e.n_queries = static_cast<uint32_t>(q_count);
-        e.query_id0 = static_cast<uint32_t>(q_begin);
-        e.exclude_self = 1;
-        e.d = static_cast<uint32_t>(d);
-        e.k = static_cast<uint32_t>(k);
-        e.out_ids = ids;
-        e.out_dists = dists;
         KNNG_TRY(launch_exact(e, metric, static_cast<uint32_t>(q_count), st));
         tk.stop(st);
         tf.start(st);
@@ -397,6 +403,48 @@ knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_
         stats->kernel_launches += launches;
     }
     return KNNG_GPU_OK;
+}
+
+knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_t n, uint64_t d, uint64_t q_begin,
+                            uint64_t q_count, uint64_t k, int metric, uint32_t* ids, float* dists, void* scratch,
+                            uint64_t scratch_bytes, cudaStream_t st, knng_gpu_stats* stats)
+{
+    if (q_begin + q_count > n) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: query range exceeds the base");
+    const uint64_t pitch = knng_gpu_padded_dim(d);
+    const U8Sets z{packed + q_begin * pitch, norms + q_begin, q_count, q_begin, packed, norms, n, 0, 1};
+    return knn_u8_sets_impl(z, d, k, metric, ids, dists, scratch, scratch_bytes, st, stats);
+}
+
+// Merge two row-wise sorted k-lists into the k best by (distance, id) -- the
+// TopK order of include/knng/top_k.hpp:56-72 -- one thread per row.
+__global__ void merge_topk_kernel(const uint32_t* __restrict__ a_ids, const float* __restrict__ a_d,
+                                  const uint32_t* __restrict__ b_ids, const float* __restrict__ b_d, uint64_t rows,
+                                  uint32_t k, uint32_t* __restrict__ o_ids, float* __restrict__ o_d)
+{
+    const uint64_t r = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    const uint64_t base = r * k;
+    uint32_t i = 0, j = 0;
+    for (uint32_t o = 0; o < k; ++o) {
+        bool take_a;
+        if (i >= k) {
+            take_a = false;
+        } else if (j >= k) {
+            take_a = true;
+        } else {
+            const int32_t ka = ordered_key(a_d[base + i]), kb = ordered_key(b_d[base + j]);
+            take_a = !key_gt(ka, a_ids[base + i], kb, b_ids[base + j]);
+        }
+        if (take_a) {
+            o_ids[base + o] = a_ids[base + i];
+            o_d[base + o] = a_d[base + i];
+            ++i;
+        } else {
+            o_ids[base + o] = b_ids[base + j];
+            o_d[base + o] = b_d[base + j];
+            ++j;
+        }
+    }
 }
 
 // ------------------------------------------------------------------ fp32 path
@@ -864,6 +912,38 @@ knng_gpu_status knng_gpu_knn_u8_noalloc(const uint8_t* d_packed, const int32_t* 
     // the previous call's contents never leak into this one.
     return knn_u8_impl(d_packed, d_norms, n, d, q_begin, q_count, k, metric, d_ids, d_dists, scratch,
                        kNoAllocScratchBytes, static_cast<cudaStream_t>(stream), stats);
+}
+
+knng_gpu_status knng_gpu_knn_u8_sets(const uint8_t* d_q_packed, const int32_t* d_q_norms, uint64_t n_q,
+                                     uint64_t q_id0, const uint8_t* d_b_packed, const int32_t* d_b_norms, uint64_t n_b,
+                                     uint64_t b_id0, uint64_t d, uint64_t k, int metric, int exclude_self,
+                                     uint32_t* d_ids, float* d_dists, void* d_scratch, uint64_t scratch_bytes,
+                                     void* stream, knng_gpu_stats* stats)
+{
+    g_last_error.clear();
+    if (k == 0) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu::brute_force_knn: k must be > 0");
+    if (k > KNNG_GPU_MAX_K)
+        return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: k exceeds the GPU limit " + std::to_string(KNNG_GPU_MAX_K));
+    if (metric != KNNG_METRIC_L2_SQUARED && metric != KNNG_METRIC_NEGATIVE_INNER_PRODUCT)
+        return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: unknown metric id " + std::to_string(metric));
+    if (d == 0 || n_b == 0) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: empty base");
+    if (q_id0 + n_q > 0xFFFFFFFFull || b_id0 + n_b > 0xFFFFFFFFull)
+        return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: ids exceed the 32-bit index_t range");
+    const U8Sets z{d_q_packed, d_q_norms, n_q, q_id0, d_b_packed, d_b_norms, n_b, b_id0, exclude_self ? 1 : 0};
+    return knn_u8_sets_impl(z, d, k, metric, d_ids, d_dists, d_scratch, scratch_bytes,
+                            static_cast<cudaStream_t>(stream), stats);
+}
+
+knng_gpu_status knng_gpu_merge_topk(const uint32_t* d_a_ids, const float* d_a_dists, const uint32_t* d_b_ids,
+                                    const float* d_b_dists, uint64_t rows, uint64_t k, uint32_t* d_out_ids,
+                                    float* d_out_dists, void* stream)
+{
+    g_last_error.clear();
+    if (rows == 0) return KNNG_GPU_OK;
+    merge_topk_kernel<<<static_cast<uint32_t>((rows + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        d_a_ids, d_a_dists, d_b_ids, d_b_dists, rows, static_cast<uint32_t>(k), d_out_ids, d_out_dists);
+    KNNG_CUDA(cudaGetLastError());
+    return KNNG_GPU_OK;
 }
 
 }  // extern "C"

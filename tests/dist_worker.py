@@ -10,7 +10,7 @@ import torch.distributed as dist
 sys.path.insert(0, os.path.join(os.path.dirname(__file__), ".."))
 import knng_gpu_b200 as kg  # noqa: E402
 from knng_gpu_b200 import synthetic as syn  # noqa: E402
-from knng_gpu_b200.distributed import ShardedBuilder  # noqa: E402
+from knng_gpu_b200.distributed import RingBuilder, ShardedBuilder  # noqa: E402
 
 
 def main():
@@ -29,6 +29,18 @@ def main():
             same = np.array_equal(ids.cpu().numpy().view(np.uint32), g.neighbors.reshape(n, k)) and \
                 np.array_equal(dists.cpu().numpy(), g.distances.reshape(n, k))
             print(f"n={n} d={d} k={k} metric={metric} world={dist.get_world_size()} equal={same}", flush=True)
+            ok &= same
+    # ring pass of base blocks (integer data)
+    for (kind, n, d, k, metric) in [(syn.KIND_SPARSE_INT, 5003, 784, 64, 1), (syn.KIND_UNIFORM_INT, 20011, 128, 10, 0)]:
+        x = syn.generate(kind, 77, n, d, p_zero=0.6)
+        rb = RingBuilder(n, d, k, metric)
+        sh = rb.shard
+        ids, dists = rb.build(torch.from_numpy(x[sh.start:sh.start + sh.count]).cuda())
+        if dist.get_rank() == 0:
+            g = kg.brute_force_knn(x, k, metric)
+            same = np.array_equal(ids.cpu().numpy().view(np.uint32), g.neighbors.reshape(n, k)) and \
+                np.array_equal(dists.cpu().numpy(), g.distances.reshape(n, k))
+            print(f"ring n={n} d={d} k={k} metric={metric} world={dist.get_world_size()} equal={same}", flush=True)
             ok &= same
     dist.barrier()
     dist.destroy_process_group()

@@ -64,3 +64,65 @@ def test_two_rank_gather_reassembles_the_graph(n):
     for p in procs:
         p.join(timeout=60)
     assert all(r[1] and r[2] for r in res), res
+
+
+def _ring_worker(rank, world, port, n, d, k, metric, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+        sys.path.insert(0, os.path.dirname(__file__))
+        from refs import oracle_knn
+        from knng_gpu_b200 import synthetic as syn
+        from knng_gpu_b200.distributed import RingBuilder
+
+        x = syn.generate(syn.KIND_UNIFORM_INT, 91, n, d)
+
+        def knn_block(q_packed, q_norms, q_id0, b_packed, b_norms, b_id0, b_count, kk, exclude_self):
+            # exact integer distances, ordered by (distance, id) like knng::TopK
+            qv = q_packed[:, :d].to(torch.int64)
+            bv = b_packed[:b_count, :d].to(torch.int64)
+            if metric == 0:
+                dd = ((qv[:, None, :] - bv[None, :, :]) ** 2).sum(-1)
+            else:
+                dd = -(qv @ bv.T)
+            gid = torch.arange(b_count, dtype=torch.int64) + b_id0
+            if exclude_self:
+                qid = torch.arange(qv.shape[0], dtype=torch.int64) + q_id0
+                dd = torch.where(gid[None, :] == qid[:, None], torch.iinfo(torch.int64).max, dd)
+            order = torch.from_numpy(np.lexsort((np.broadcast_to(gid.numpy(), dd.shape), dd.numpy()), axis=1))
+            sel = order[:, :kk]
+            return (gid[sel].to(torch.int32), torch.gather(dd, 1, sel).to(torch.float32))
+
+        def merge(a_ids, a_d, b_ids, b_d):
+            ids = torch.cat([a_ids, b_ids], 1).numpy().view(np.uint32).astype(np.int64)
+            ds = torch.cat([a_d, b_d], 1).numpy()
+            order = np.lexsort((ids, ds), axis=1)[:, :k]
+            return (torch.from_numpy(np.take_along_axis(ids, order, 1).astype(np.uint32).view(np.int32)),
+                    torch.from_numpy(np.take_along_axis(ds, order, 1)))
+
+        rb = RingBuilder(n, d, k, metric, knn_block=knn_block, merge=merge, device=torch.device("cpu"))
+        sh = rb.shard
+        ids, dists = rb.build(torch.from_numpy(x[sh.start:sh.start + sh.count]))
+        full_ids, full_d = oracle_knn(x, k, metric)
+        q.put((rank, bool(np.array_equal(ids.numpy().view(np.uint32), full_ids)),
+               bool(np.array_equal(dists.numpy(), full_d))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,n,k,metric", [(2, 101, 5, 0), (3, 64, 7, 1), (3, 20, 9, 0)])
+def test_ring_schedule_reassembles_the_graph(world, n, k, metric):
+    """The ring schedule (send right, receive left, merge per block) gives the
+    single-process oracle graph, including blocks smaller than k."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + n + world
+    procs = [ctx.Process(target=_ring_worker, args=(r, world, port, n, 8, k, metric, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=180) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(r[1] and r[2] for r in res), res
