@@ -126,6 +126,8 @@ def synth_lib() -> ctypes.CDLL:
         lib.knng_synth_generate.restype = c_int
         lib.knng_synth_generate.argtypes = [c_int, c_uint64, c_uint64, c_uint64, c_void_p, c_uint64, c_float,
                                             c_float, c_void_p]
+        lib.knng_dataset_hash.restype = c_uint64
+        lib.knng_dataset_hash.argtypes = [c_void_p, c_uint64, c_uint64]
         lib.knng_synth_sample_ids.restype = c_int
         lib.knng_synth_sample_ids.argtypes = [c_uint64, c_uint64, c_uint64, c_void_p]
         _synth = lib

@@ -53,9 +53,23 @@ def build_synth(verbose: bool = False, force: bool = False) -> Path:
     return out
 
 
+def build_cli(verbose: bool = False, force: bool = False) -> Path:
+    """build_knng_gpu: the reference's build_knng CLI over libknng_gpu.so."""
+    out = PKG / "bin" / "build_knng_gpu"
+    srcs = [PKG / "cli" / "build_knng_gpu.cpp", PKG / "cli" / "knng_files.hpp", ROOT / "include" / "knng_gpu.h",
+            PKG / "libknng_gpu.so"]
+    if force or _stale(out, srcs):
+        out.parent.mkdir(exist_ok=True)
+        _run(["g++", "-std=c++17", "-O2", f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include", "-o", str(out),
+              str(PKG / "cli" / "build_knng_gpu.cpp"), f"-L{PKG}", "-lknng_gpu", "-L/usr/local/cuda/lib64",
+              "-lcudart", "-Wl,-rpath,$ORIGIN/..:/usr/local/cuda/lib64"], verbose)
+    return out
+
+
 def build_all(verbose: bool = False, force: bool = False) -> None:
     build_synth(verbose, force)
     build_gpu(verbose, force)
+    build_cli(verbose, force)
 
 
 if __name__ == "__main__":

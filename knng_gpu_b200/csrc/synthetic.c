@@ -1,6 +1,6 @@
 /*
  * synthetic.c -- seeded synthetic datasets for the benchmark configurations
- * (host C, libknng_synth.so). Every dataset is drawn row-major from one
+ * and the dataset hash (host C, libknng_synth.so). Every dataset is drawn row-major from one
  * knng::random::XorShift64 stream (include/knng/random.hpp:48-144): the
  * (13, 7, 17) xorshift, next_float01 = top 24 bits / 2^24, next_below =
  * Lemire multiply-high, as in the reference's bench generator
@@ -119,4 +119,19 @@ int knng_synth_sample_ids(uint64_t seed, uint64_t n, uint64_t count, uint64_t *o
         if (bits[i >> 6] & (1ull << (i & 63))) out[w++] = i;
     free(bits);
     return 0;
+}
+
+/* FNV-1a 64 dataset hash over (u64 n, u64 d, fp32 payload): the key of the
+ * ground-truth cache (src/bench/ground_truth.cpp:45-56, 90-101). */
+uint64_t knng_dataset_hash(const float *x, uint64_t n, uint64_t d)
+{
+    uint64_t s = 14695981039346656037ull;
+    const unsigned char *p;
+    p = (const unsigned char *)&n;
+    for (int i = 0; i < 8; ++i) { s ^= p[i]; s *= 1099511628211ull; }
+    p = (const unsigned char *)&d;
+    for (int i = 0; i < 8; ++i) { s ^= p[i]; s *= 1099511628211ull; }
+    p = (const unsigned char *)x;
+    for (uint64_t i = 0; i < n * d * 4; ++i) { s ^= p[i]; s *= 1099511628211ull; }
+    return s;
 }

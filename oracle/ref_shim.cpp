@@ -167,3 +167,47 @@ uint64_t ref_topk_run(uint64_t k, uint64_t count, const uint32_t* ids, const flo
 }
 
 }  // extern "C"
+
+// File-format hooks: the reference's loaders and ground-truth writer.
+#include "knng/io/fvecs.hpp"
+extern "C" {
+// kind 0 fvecs, 1 ivecs, 2 bvecs. Returns 0 and fills n/d (and out when
+// non-NULL, sized n*d elements); 1 with the message in ref_last_error.
+int ref_load_vecs(const char* path, int kind, void* out, uint64_t* n, uint64_t* d)
+{
+    try {
+        if (kind == 0) {
+            const knng::Dataset ds = knng::io::load_fvecs(path);
+            *n = ds.n; *d = ds.d;
+            if (out) std::memcpy(out, ds.data.data(), ds.data.size() * 4);
+        } else if (kind == 1) {
+            const auto ds = knng::io::load_ivecs(path);
+            *n = ds.n; *d = ds.d;
+            if (out) std::memcpy(out, ds.data.data(), ds.data.size() * 4);
+        } else {
+            const auto ds = knng::io::load_bvecs(path);
+            *n = ds.n; *d = ds.d;
+            if (out) std::memcpy(out, ds.data.data(), ds.data.size());
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return 1;
+    }
+}
+
+int ref_save_ground_truth(const char* path, const uint32_t* ids, const float* dists, uint64_t n, uint64_t k,
+                          uint64_t hash, int metric)
+{
+    try {
+        knng::Knng g(n, k);
+        std::memcpy(g.neighbors.data(), ids, n * k * 4);
+        std::memcpy(g.distances.data(), dists, n * k * 4);
+        knng::bench::save_ground_truth(path, g, hash, static_cast<knng::bench::MetricId>(metric));
+        return 0;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return 1;
+    }
+}
+}  // extern "C"
