@@ -259,12 +259,12 @@ def main() -> None:
     achieved = shard_ops / (kms * 1e-3) / 1e12
     traffic = None
     try:
-        tj = json.loads((ROOT / "profiles" / "knn_u8_tc_traffic.json").read_text())
+        tj = json.loads((ROOT / "profiles" / "knn_tc_u8_cfg3_traffic.json").read_text())
         traffic = float(tj["dram_bytes_per_launch_full_cfg3"]) * builder.shard.count / n
     except Exception:
         pass
     roofline = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
-                "frac": achieved / int8_peak, "traffic": traffic, "kernel": "knn_u8_tc_kernel",
+                "frac": achieved / int8_peak, "traffic": traffic, "kernel": "knn_tc_kernel<ElemU8,...>",
                 "kernel_ms": kms, "peak_basis": peak_src}
 
     # ---- parity spot check: 4 rows recomputed in float64 with torch (exact

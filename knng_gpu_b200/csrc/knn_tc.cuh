@@ -29,6 +29,7 @@
 #pragma once
 #include <climits>
 #include <cstdint>
+#include <type_traits>
 
 #include "ptx.cuh"
 #include "topk.cuh"
@@ -39,16 +40,19 @@ constexpr int kTileRows = 128;      // M per UMMA, N per base tile, rows per TMA
 constexpr int kChunkBytes = 128;    // K bytes per TMA box / swizzle atom
 constexpr int kBoxBytes = kTileRows * kChunkBytes;  // 16 KiB
 constexpr int kSlowPitch = 36;      // ints per thread in the slow-path spill area
+constexpr int kNormRing = 4;        // base-tile norm slots per epilogue warp (prefetch depth + 1)
+// Software-pipelined TMEM loads in the epilogue (measured slower at d = 128).
+constexpr bool kPipelineTmemLoads = false;
 
 struct ElemU8 {
     static constexpr int kPlanes = 1;
     static constexpr bool kFloat = false;
     __device__ static uint32_t idesc() { return idesc_u8_s32(kTileRows, kTileRows); }
-    // One K step = 32 bytes of each operand.
-    __device__ static void mma_step(uint32_t d, const uint32_t* a, const uint32_t* b, uint32_t off, uint32_t idesc,
-                                    bool accumulate)
+    // One K step = 32 bytes of each operand; a/b are smem descriptors.
+    __device__ static void mma_step(uint32_t d, const uint64_t* a, const uint64_t* b, uint32_t idesc,
+                                    uint32_t accumulate)
     {
-        umma_u8(d, umma_desc_sw128(a[0] + off), umma_desc_sw128(b[0] + off), idesc, accumulate);
+        umma_u8(d, a[0], b[0], idesc, accumulate);
     }
 };
 
@@ -56,12 +60,12 @@ struct ElemBf16x3 {
     static constexpr int kPlanes = 2;  // hi, lo
     static constexpr bool kFloat = true;
     __device__ static uint32_t idesc() { return idesc_bf16_f32(kTileRows, kTileRows); }
-    __device__ static void mma_step(uint32_t d, const uint32_t* a, const uint32_t* b, uint32_t off, uint32_t idesc,
-                                    bool accumulate)
+    __device__ static void mma_step(uint32_t d, const uint64_t* a, const uint64_t* b, uint32_t idesc,
+                                    uint32_t accumulate)
     {
-        umma_f16(d, umma_desc_sw128(a[0] + off), umma_desc_sw128(b[0] + off), idesc, accumulate);  // hi.hi
-        umma_f16(d, umma_desc_sw128(a[0] + off), umma_desc_sw128(b[1] + off), idesc, true);        // hi.lo
-        umma_f16(d, umma_desc_sw128(a[1] + off), umma_desc_sw128(b[0] + off), idesc, true);        // lo.hi
+        umma_f16(d, a[0], b[0], idesc, accumulate);  // hi.hi
+        umma_f16(d, a[0], b[1], idesc, 1u);          // hi.lo
+        umma_f16(d, a[1], b[0], idesc, 1u);          // lo.hi
     }
 };
 
@@ -84,26 +88,30 @@ struct KnnTcParams {
     uint32_t* fallback_count;
     int* error;                  // non-zero: a bounded wait gave up
     uint32_t debug_flags;        // profiling only: 1 skip filtering, 2 skip insertion, 4 skip TMEM loads
+    unsigned long long* debug_clocks;  // profiling only: per-role wait cycles (flag 512)
 };
 
 struct SmemLayoutTc {
-    uint32_t a_off, b_off, nb_off, slow_off, bar_off, total, stage_bytes, a_bytes;
+    uint32_t a_off, b_off, nb_off, slow_off, merge_off, bar_off, total, stage_bytes, a_bytes;
 };
 
+// split: epilogue warps per (M tile, TMEM lane quarter), each covering
+// 1/split of the columns; their lists meet in `merge` (2 * kcap ints per row).
 __host__ __device__ inline SmemLayoutTc smem_layout_tc(int planes, int mt, bool a_stream, uint32_t kchunks,
-                                                       uint32_t stages)
+                                                       uint32_t stages, int split = 1, int kcap = 0)
 {
     SmemLayoutTc L;
     // A resident: all K chunks of MT tiles. A streamed: a stage carries the
     // A chunk(s) next to the B chunk.
     L.a_bytes = a_stream ? 0 : mt * kchunks * planes * kBoxBytes;
     L.stage_bytes = (a_stream ? mt + 1 : 1) * planes * kBoxBytes;
-    const int epi_threads = mt * kTileRows;
+    const int epi_threads = mt * kTileRows * split;
     L.a_off = 0;
     L.b_off = L.a_off + L.a_bytes;
     L.nb_off = L.b_off + stages * L.stage_bytes;
-    L.slow_off = L.nb_off + (epi_threads / 32) * 2 * kTileRows * 4;  // per epilogue warp, double-buffered
-    L.bar_off = L.slow_off + epi_threads * kSlowPitch * 4;
+    L.slow_off = L.nb_off + (epi_threads / 32) * kNormRing * kTileRows * 4;  // per epilogue warp ring
+    L.merge_off = L.slow_off + epi_threads * kSlowPitch * 4;
+    L.bar_off = L.merge_off + (split > 1 ? mt * kTileRows * 2 * kcap * 4 : 0);
     L.total = L.bar_off + 512;  // barriers + tmem slot + abort flag + stage counter
     return L;
 }
@@ -128,8 +136,8 @@ __device__ __forceinline__ int32_t tree_min(const int32_t* v)
 // Order-preserving int image of an fp32 key, branch-free (finite or +inf).
 __device__ __forceinline__ int32_t ordered_bits(int32_t b) { return b ^ ((b >> 31) & 0x7FFFFFFF); }
 
-template <class Elem, int MT, int NBUF, bool A_STREAM, int METRIC, class TopK>
-__global__ void __launch_bounds__(64 + 128 * MT, 1)
+template <class Elem, int MT, int NBUF, bool A_STREAM, int METRIC, class TopK, int SPLIT>
+__global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
     knn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q0, const __grid_constant__ CUtensorMap tmap_q1,
                   const __grid_constant__ CUtensorMap tmap_b0, const __grid_constant__ CUtensorMap tmap_b1,
                   const KnnTcParams p)
@@ -143,10 +151,15 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
     // two TMEM buffers all M tiles of a base tile share one handoff barrier;
     // with one buffer each M tile gets its own so the two tiles alternate.
     constexpr bool kPerMtBars = NBUF == 1 && MT > 1;
+    // SPLIT == 2: two epilogue warps per TMEM lane quarter (four per SM
+    // sub-partition instead of two), each filtering half of every tile's
+    // columns into its own list; the halves merge at the end of a query tile.
+    static_assert(SPLIT == 1 || (SPLIT == 2 && TopK::kRegs <= 32 && !kPerMtBars), "split epilogue");
+    constexpr int kCap = TopK::kRegs / 2;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const SmemLayoutTc L = smem_layout_tc(P, MT, A_STREAM, p.kchunks, p.stages);
+    const SmemLayoutTc L = smem_layout_tc(P, MT, A_STREAM, p.kchunks, p.stages, SPLIT, SPLIT > 1 ? kCap : 0);
     uint8_t* sA = smem + L.a_off;
     uint8_t* sB = smem + L.b_off;
     int32_t* sNB = reinterpret_cast<int32_t*>(smem + L.nb_off);
@@ -166,6 +179,9 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
     // tile that read it is counted here, so the MMA warp issues one
     // tcgen05.commit per tile (the TMEM handoff) instead of two.
     volatile uint32_t* tiles_done = reinterpret_cast<volatile uint32_t*>(bars + 48);
+    uint64_t* merge_full = bars + 50;   // [MT]
+    uint64_t* merge_empty = bars + 52;  // [MT]
+    int32_t* sMerge = reinterpret_cast<int32_t*>(smem + L.merge_off);
     // With fewer stages than two tiles' worth of K chunks a tile cannot wait
     // for a whole earlier tile, so stages are released per chunk instead.
     const bool stage_commits = p.stages < 2 * p.kchunks;
@@ -185,10 +201,15 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
         mbar_init(a_empty, 1);
         for (int b = 0; b < NBUF * MT; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], kPerMtBars ? 4 : 4 * MT);
+            mbar_init(&tempty[b], kPerMtBars ? 4 : 4 * MT * SPLIT);
         }
         *abort_flag = 0;
         *tiles_done = 0;
+        mbar_init(&bars[60], 1);
+        for (int m = 0; m < MT; ++m) {
+            mbar_init(&merge_full[m], 4);
+            mbar_init(&merge_empty[m], 4);
+        }
         fence_barrier_init();
         prefetch_tensormap(&tmap_q0);
         prefetch_tensormap(&tmap_b0);
@@ -210,6 +231,8 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
             const CUtensorMap* bmap[2] = {&tmap_b0, &tmap_b1};
             uint32_t stage = 0, phase = 0, a_par = 0, load_idx = 0;
             bool ok = true;
+            const bool dbg = (p.debug_flags & 512u) && p.debug_clocks;
+            long long c_wait = 0, c_start = clock64();
             for (uint32_t t = blockIdx.x; t < n_qtiles && ok; t += gridDim.x) {
                 if (!A_STREAM) {
                     ok = mbar_wait(a_empty, a_par ^ 1, abort_flag);
@@ -231,7 +254,9 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
                         } else if (load_idx >= S) {
                             // The stage last held load (load_idx - S), part of
                             // tile (load_idx - S) / kchunks.
+                            const long long w0 = clock64();
                             ok = spin_until_geq(tiles_done, (load_idx - S) / p.kchunks + 1, abort_flag);
+                            c_wait += clock64() - w0;
                             if (!ok) break;
                         }
                         ++load_idx;
@@ -252,6 +277,10 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
                     }
                 }
             }
+            if (dbg) {
+                atomicAdd(p.debug_clocks + 5, static_cast<unsigned long long>(c_wait));
+                atomicAdd(p.debug_clocks + 6, static_cast<unsigned long long>(clock64() - c_start));
+            }
             if (!ok) {
                 atomicOr(p.error, 1);
                 *abort_flag = 1;
@@ -259,16 +288,39 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------ UMMA issuer
+        // One thread issues every MMA of the CTA, so its loop is kept lean:
+        // descriptors are precomputed and advanced by adding (byte offset
+        // >> 4) to the start-address field, stage/phase counters advance
+        // incrementally, and nothing is divided.
         if (lane == 0) {
             const uint32_t idesc = Elem::idesc();
-            uint32_t stage0 = 0, phase0 = 0, a_par = 0, acc_i = 0;
+            const uint64_t a_desc0 = umma_desc_sw128(smem_u32(sA));
+            const uint64_t b_desc0 = umma_desc_sw128(smem_u32(sB));
+            constexpr uint64_t kBoxStep = kBoxBytes >> 4;  // descriptor units per 16 KiB box
+            const uint64_t stage_step = stage_bytes >> 4;
+            uint32_t s = 0, ph = 0, a_par = 0, acc_i = 0;
             bool ok = true;
-            const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
-            // Operand plane addresses of M tile mt / the B tile in stage s.
-            auto a_planes = [&](int mt, uint32_t kc, uint32_t s, uint32_t* a) {
-                for (int pl = 0; pl < P; ++pl)
-                    a[pl] = A_STREAM ? b_base + s * stage_bytes + ((1 + mt) * P + pl) * kBoxBytes
-                                     : a_base + ((mt * p.kchunks + kc) * P + pl) * kBoxBytes;
+            const bool dbg = (p.debug_flags & 512u) && p.debug_clocks;
+            const bool no_mma = (p.debug_flags & 128u) != 0;  // profiling: epilogue without MMAs
+            long long c_tempty = 0, c_full = 0, c_start = clock64();
+            // Issue the K steps of one 128-byte K chunk for M tile mt.
+            auto issue_chunk = [&](uint32_t d_tmem, int mt, uint32_t kc, uint32_t stage, bool first) {
+                uint64_t a[2], b[2];
+#pragma unroll
+                for (int pl = 0; pl < P; ++pl) {
+                    a[pl] = A_STREAM ? b_desc0 + stage * stage_step + ((1 + mt) * P + pl) * kBoxStep
+                                     : a_desc0 + ((mt * p.kchunks + kc) * P + pl) * kBoxStep;
+                    b[pl] = b_desc0 + stage * stage_step + pl * kBoxStep;
+                }
+#pragma unroll
+                for (int ks = 0; ks < kChunkBytes / 32; ++ks) {
+                    if (!no_mma) Elem::mma_step(d_tmem, a, b, idesc, (first && ks == 0) ? 0u : 1u);
+#pragma unroll
+                    for (int pl = 0; pl < P; ++pl) {
+                        a[pl] += 2;  // 32 bytes
+                        b[pl] += 2;
+                    }
+                }
             };
             for (uint32_t t = blockIdx.x; t < n_qtiles && ok; t += gridDim.x) {
                 if (!A_STREAM) {
@@ -278,64 +330,79 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
                     tc_fence_after();
                 }
                 for (uint32_t j = 0; j < n_btiles && ok; ++j, ++acc_i) {
-                    const uint32_t buf = acc_i % NBUF;
+                    const uint32_t buf = NBUF == 1 ? 0u : acc_i & (NBUF - 1);
                     const uint32_t tpar = (acc_i / NBUF) & 1;
                     if (kPerMtBars) {
                         // One buffer per M tile: M tile mt waits for its own
-                        // epilogue; a B stage is released after the last M tile.
+                        // epilogue; a B stage is released after the last M tile
+                        // (the host keeps kchunks <= 2 here).
+                        uint32_t st_k[2] = {s, s}, ph_k[2] = {ph, ph};
+                        {
+                            uint32_t s2 = s, ph2 = ph;
+                            for (uint32_t kc = 0; kc < p.kchunks && kc < 2; ++kc) {
+                                st_k[kc] = s2;
+                                ph_k[kc] = ph2;
+                                if (++s2 == S) {
+                                    s2 = 0;
+                                    ph2 ^= 1;
+                                }
+                            }
+                            s = s2;
+                            ph = ph2;
+                        }
                         for (int mt = 0; mt < MT && ok; ++mt) {
+                            const long long w0 = clock64();
                             ok = mbar_wait(&tempty[mt], tpar ^ 1, abort_flag);
+                            c_tempty += clock64() - w0;
                             if (!ok) break;
                             tc_fence_after();
-                            const uint32_t d_tmem = tmem_base + mt * BN;
-                            for (uint32_t kc = 0; kc < p.kchunks; ++kc) {
-                                const uint32_t idx = stage0 + kc;
-                                const uint32_t s = idx % S;
+                            for (uint32_t kc = 0; kc < p.kchunks && kc < 2; ++kc) {
                                 if (mt == 0) {
-                                    ok = mbar_wait(&full[s], phase0 ^ ((idx / S) & 1), abort_flag);
+                                    const long long w1 = clock64();
+                                    ok = mbar_wait(&full[st_k[kc]], ph_k[kc], abort_flag);
+                                    c_full += clock64() - w1;
                                     if (!ok) break;
                                     tc_fence_after();
                                 }
-                                uint32_t a[2], b[2];
-                                a_planes(mt, kc, s, a);
-                                for (int pl = 0; pl < P; ++pl) b[pl] = b_base + s * stage_bytes + pl * kBoxBytes;
-#pragma unroll
-                                for (int ks = 0; ks < kChunkBytes / 32; ++ks)
-                                    Elem::mma_step(d_tmem, a, b, ks * 32, idesc, (kc | ks) != 0);
-                                if (stage_commits && mt == MT - 1) umma_commit(&empty[s]);
+                                issue_chunk(tmem_base + mt * BN, mt, kc, st_k[kc], kc == 0);
+                                if (stage_commits && mt == MT - 1) umma_commit(&empty[st_k[kc]]);
                             }
                             if (ok) umma_commit(&tfull[mt]);
                         }
                     } else {
-                        ok = mbar_wait(&tempty[buf], tpar ^ 1, abort_flag);
-                        if (!ok) break;
+                        // debug 64 (profiling with an idle epilogue only): do not wait for the handoff
+                        if (!(p.debug_flags & 64u)) {
+                            const long long w0 = clock64();
+                            ok = mbar_wait(&tempty[buf], tpar ^ 1, abort_flag);
+                            c_tempty += clock64() - w0;
+                            if (!ok) break;
+                        }
                         tc_fence_after();
                         for (uint32_t kc = 0; kc < p.kchunks && ok; ++kc) {
-                            const uint32_t idx = stage0 + kc;
-                            const uint32_t s = idx % S;
-                            ok = mbar_wait(&full[s], phase0 ^ ((idx / S) & 1), abort_flag);
+                            const long long w1 = clock64();
+                            ok = mbar_wait(&full[s], ph, abort_flag);
+                            c_full += clock64() - w1;
                             if (!ok) break;
                             tc_fence_after();
-                            uint32_t b[2];
-                            for (int pl = 0; pl < P; ++pl) b[pl] = b_base + s * stage_bytes + pl * kBoxBytes;
 #pragma unroll
-                            for (int mt = 0; mt < MT; ++mt) {
-                                uint32_t a[2];
-                                a_planes(mt, kc, s, a);
-                                const uint32_t d_tmem = tmem_base + (buf * MT + mt) * BN;
-#pragma unroll
-                                for (int ks = 0; ks < kChunkBytes / 32; ++ks)
-                                    Elem::mma_step(d_tmem, a, b, ks * 32, idesc, (kc | ks) != 0);
-                            }
+                            for (int mt = 0; mt < MT; ++mt)
+                                issue_chunk(tmem_base + (buf * MT + mt) * BN, mt, kc, s, kc == 0);
                             if (stage_commits) umma_commit(&empty[s]);
+                            if (++s == S) {
+                                s = 0;
+                                ph ^= 1;
+                            }
                         }
                         if (ok) umma_commit(&tfull[buf]);
+                        if (p.debug_flags & 32u) umma_commit(&bars[60]);  // profiling: one extra commit per tile
                     }
-                    const uint32_t next = stage0 + p.kchunks;
-                    phase0 ^= (next / S) & 1;
-                    stage0 = next % S;
                 }
                 if (ok && !A_STREAM) umma_commit(a_empty);
+            }
+            if (dbg) {
+                atomicAdd(p.debug_clocks + 0, static_cast<unsigned long long>(c_tempty));
+                atomicAdd(p.debug_clocks + 1, static_cast<unsigned long long>(c_full));
+                atomicAdd(p.debug_clocks + 2, static_cast<unsigned long long>(clock64() - c_start));
             }
             if (!ok) {
                 atomicOr(p.error, 2);
@@ -345,26 +412,39 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
     } else {
         // ------------------------------------------------ epilogue
         const int ew = warp - 2;
-        const int mt = ew >> 2;
+        const int grp = ew >> 2;
+        const int mt = grp % MT;
+        const int half = grp / MT;  // which 1/SPLIT of the columns
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
-        int32_t* nbuf = sNB + ew * 2 * BN;  // this warp's copy of the base-tile norms
+        int32_t* nbuf = sNB + ew * kNormRing * BN;  // this warp's ring of base-tile norms
         int32_t* slow = sSlow + (ew * 32 + lane) * kSlowPitch;
         // Per-column addend of the key: u8 L2 |r|^2, bf16x3 L2 |r'|^2 (fp32
         // bits), 0 for inner product; padding rows (dot == 0 there) get
         // INT_MAX (u8) or +inf (bf16x3), so they never beat a real row.
         const int32_t kPad = Elem::kFloat ? 0x7F800000 : INT_MAX;
-        auto load_norms = [&](uint32_t j) -> int4 {
+        // Norms of base tile j reach slot j % kNormRing by cp.async issued
+        // kNormRing - 1 tiles ahead (no register dependency, so the global
+        // latency never stalls the epilogue); lane l covers columns 4l..4l+3.
+        auto fetch_norms = [&](uint32_t j) {
+            int32_t* dst = nbuf + (j % kNormRing) * BN + lane * 4;
             const uint64_t b0 = static_cast<uint64_t>(j) * BN + lane * 4;
-            const int32_t* nb = static_cast<const int32_t*>(p.base_norms);
-            if (b0 + 3 < p.n_base)
-                return METRIC == 0 ? __ldg(reinterpret_cast<const int4*>(nb + b0)) : make_int4(0, 0, 0, 0);
-            int4 nn;
-            nn.x = b0 + 0 < p.n_base ? (METRIC == 0 ? nb[b0 + 0] : 0) : kPad;
-            nn.y = b0 + 1 < p.n_base ? (METRIC == 0 ? nb[b0 + 1] : 0) : kPad;
-            nn.z = b0 + 2 < p.n_base ? (METRIC == 0 ? nb[b0 + 2] : 0) : kPad;
-            nn.w = b0 + 3 < p.n_base ? (METRIC == 0 ? nb[b0 + 3] : 0) : kPad;
-            return nn;
+            if (METRIC == 0) {
+                const uint64_t valid = b0 < p.n_base ? (p.n_base - b0 < 4 ? p.n_base - b0 : 4) : 0;
+                const int32_t* src = static_cast<const int32_t*>(p.base_norms) + (valid ? b0 : 0);
+                cp_async_16_zfill(dst, src, static_cast<uint32_t>(valid * 4));
+            }
+        };
+        // Columns past the base (last tile only) and inner-product tiles are
+        // written directly once the copies of tile j have landed.
+        auto finish_norms = [&](uint32_t j) {
+            int32_t* dst = nbuf + (j % kNormRing) * BN + lane * 4;
+            const uint64_t b0 = static_cast<uint64_t>(j) * BN + lane * 4;
+            if (METRIC != 0 || b0 + 3 >= p.n_base) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (METRIC != 0 || b0 + e >= p.n_base) dst[e] = b0 + e < p.n_base ? 0 : kPad;
+            }
         };
         // The key of one column from its accumulator and norm addend.
         auto key_of = [](int32_t acc, int32_t nb) -> int32_t {
@@ -375,9 +455,13 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
                 return METRIC == 0 ? nb - 2 * acc : nb - acc;
             }
         };
+        int32_t* merge_slot = sMerge + (mt * kTileRows + row) * 2 * kCap;
+        uint32_t qt_iter = 0;
         uint32_t acc_i = 0;
         bool ok = true;
-        for (uint32_t t = blockIdx.x; t < n_qtiles && ok; t += gridDim.x) {
+        const bool dbg = (p.debug_flags & 512u) && p.debug_clocks && ew == 0 && lane == 0;
+        long long c_tfull = 0, c_start = clock64();
+        for (uint32_t t = blockIdx.x; t < n_qtiles && ok; t += gridDim.x, ++qt_iter) {
             const uint32_t qlocal = (t * MT + mt) * kTileRows + row;
             const bool qvalid = qlocal < p.n_queries;
             const uint32_t self_id = p.exclude_self ? p.query_id0 + qlocal : UINT32_MAX;
@@ -385,57 +469,51 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
             TopK tk;
             tk.init(p.k);
             int32_t thr = tk.thr();
-            int4 nn_next = load_norms(0);
+            __syncwarp();
+            for (uint32_t jj = 0; jj + 1 < kNormRing; ++jj) {
+                if (jj < n_btiles) fetch_norms(jj);
+                cp_async_commit();
+            }
             for (uint32_t j = 0; j < n_btiles; ++j, ++acc_i) {
-                // Publish this tile's norms (fetched one tile earlier) and
-                // start fetching the next tile's, so the global latency hides
-                // behind a whole tile of work.
-                reinterpret_cast<int4*>(nbuf + (j & 1) * BN)[lane] = nn_next;
-                if (j + 1 < n_btiles) nn_next = load_norms(j + 1);
+                // Every lane is done with tile j-1, whose slot now receives
+                // tile j + kNormRing - 1; then wait for tile j's copies.
+                __syncwarp();
+                if (j + kNormRing - 1 < n_btiles) fetch_norms(j + kNormRing - 1);
+                cp_async_commit();
+                cp_async_wait_group<kNormRing - 1>();
+                finish_norms(j);
                 __syncwarp();
                 const uint32_t buf = acc_i % NBUF;
                 const uint32_t hb = kPerMtBars ? mt : buf;  // handoff barrier
-                ok = mbar_wait(&tfull[hb], (acc_i / NBUF) & 1, abort_flag);
+                const long long w0 = clock64();
+                ok = (p.debug_flags & 256u) ? mbar_wait_spin(&tfull[hb], (acc_i / NBUF) & 1, abort_flag)
+                                                : mbar_wait(&tfull[hb], (acc_i / NBUF) & 1, abort_flag);
+                c_tfull += clock64() - w0;
                 if (!ok) break;
                 tc_fence_after();
                 if (ew == (kPerMtBars ? 4 * (MT - 1) : 0) && lane == 0) *tiles_done = acc_i + 1;
-                const uint32_t tb =
-                    tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + (buf * MT + mt) * BN;
-                const int4* nb4 = reinterpret_cast<const int4*>(nbuf + (j & 1) * BN);
-                // Steps of kW columns: one TMEM wait per step, all keys of the
-                // step computed before one threshold test (ILP over kW keys).
-                constexpr int kW = TopK::kRegs <= 64 ? 64 : 32;
+                const uint32_t tb = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + (buf * MT + mt) * BN +
+                                    half * (BN / SPLIT);
+                constexpr int kCols = BN / SPLIT;  // columns of each tile this thread filters
+                const int4* nb4 = reinterpret_cast<const int4*>(nbuf + (j % kNormRing) * BN + half * kCols);
+                // Keys of W columns (starting at column c0 of the tile), one
+                // threshold test on their minimum, and the rare insertion path:
+                // spill the keys and insert those under the running threshold,
+                // in id order.
+                auto filter = [&](int32_t* v, auto w_tag, int c0) {
+                    constexpr int W = decltype(w_tag)::value;
 #pragma unroll
-                for (int st = 0; st < BN / kW; ++st) {
-                    int32_t v[kW];
-                    __syncwarp();
-                    if (!(p.debug_flags & 4u)) {
-#pragma unroll
-                        for (int c = 0; c < kW / 32; ++c) tmem_ld_32cols(tb + st * kW + c * 32, v + c * 32);
-                        tmem_ld_wait_n<kW>(v);
-                    }
-                    if (st + 1 == BN / kW) {
-                        // Every column of this buffer is in registers: hand it
-                        // back to the MMA warp before the last filtering step.
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&tempty[hb]);
-                    }
-                    if (p.debug_flags & 1u) continue;
-#pragma unroll
-                    for (int i4 = 0; i4 < kW / 4; ++i4) {
-                        const int4 nn = nb4[st * kW / 4 + i4];
+                    for (int i4 = 0; i4 < W / 4; ++i4) {
+                        const int4 nn = nb4[c0 / 4 + i4];
                         v[4 * i4 + 0] = key_of(v[4 * i4 + 0], nn.x);
                         v[4 * i4 + 1] = key_of(v[4 * i4 + 1], nn.y);
                         v[4 * i4 + 2] = key_of(v[4 * i4 + 2], nn.z);
                         v[4 * i4 + 3] = key_of(v[4 * i4 + 3], nn.w);
                     }
-                    const int32_t step_min = tree_min<kW>(v);  // depth log3(kW)
+                    const int32_t step_min = tree_min<W>(v);  // depth log3(W)
                     if (step_min < thr && !(p.debug_flags & 2u)) {
-                        // Rare path, per 32 columns: spill the keys and insert
-                        // those under the running threshold, in id order.
 #pragma unroll
-                        for (int c = 0; c < kW / 32; ++c) {
+                        for (int c = 0; c < W / 32; ++c) {
                             const int32_t* vc = v + c * 32;
                             uint32_t mask = 0;
 #pragma unroll
@@ -445,7 +523,7 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
                             for (int i4 = 0; i4 < 8; ++i4)
                                 *reinterpret_cast<int4*>(slow + 4 * i4) =
                                     make_int4(vc[4 * i4], vc[4 * i4 + 1], vc[4 * i4 + 2], vc[4 * i4 + 3]);
-                            const uint32_t col0 = p.base_id0 + j * BN + st * kW + c * 32;
+                            const uint32_t col0 = p.base_id0 + j * BN + half * kCols + c0 + c * 32;
                             while (mask) {
                                 const int i = __ffs(mask) - 1;
                                 mask &= mask - 1;
@@ -458,9 +536,85 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
                             }
                         }
                     }
+                };
+                auto release = [&]() {
+                    // Every column of this buffer is in registers: hand it back
+                    // to the MMA warp before the last filtering step.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[hb]);
+                };
+                const bool loads = !(p.debug_flags & 4u), filtering = !(p.debug_flags & 1u);
+                if constexpr (TopK::kRegs <= 32 && kPipelineTmemLoads) {
+                    // Small lists: 32-column chunks, software-pipelined -- the
+                    // TMEM load of chunk c+1 is in flight while chunk c is
+                    // filtered (two epilogue warps per sub-partition cannot
+                    // hide the load latency otherwise).
+                    int32_t va[32], vb[32];
+                    __syncwarp();
+                    if (loads) {
+                        tmem_ld_32cols(tb, va);
+                        tmem_ld_wait_n<32>(va);
+                    }
+#pragma unroll
+                    for (int c = 0; c < kCols / 32; ++c) {
+                        int32_t* vc = (c & 1) ? vb : va;
+                        int32_t* vn = (c & 1) ? va : vb;
+                        if (c + 1 < kCols / 32) {
+                            __syncwarp();
+                            if (loads) tmem_ld_32cols(tb + (c + 1) * 32, vn);
+                        } else {
+                            release();
+                        }
+                        if (filtering) filter(vc, std::integral_constant<int, 32>{}, c * 32);
+                        if (c + 1 < kCols / 32) {
+                            __syncwarp();
+                            if (loads) tmem_ld_wait_n<32>(vn);
+                        }
+                    }
+                } else {
+                    // Larger lists: steps of kW columns, one TMEM wait per step.
+                    constexpr int kW = (SPLIT == 1 && TopK::kRegs <= 64) ? 64 : 32;
+#pragma unroll
+                    for (int st = 0; st < kCols / kW; ++st) {
+                        int32_t v[kW];
+                        __syncwarp();
+                        if (loads) {
+#pragma unroll
+                            for (int c = 0; c < kW / 32; ++c) tmem_ld_32cols(tb + st * kW + c * 32, v + c * 32);
+                            tmem_ld_wait_n<kW>(v);
+                        }
+                        if (st + 1 == kCols / kW) release();
+                        if (filtering) filter(v, std::integral_constant<int, kW>{}, st * kW);
+                    }
                 }
             }
             if (!ok) break;
+            if constexpr (SPLIT > 1) {
+                // Merge the column halves: half 1 publishes its list, half 0
+                // inserts it (ids interleave, so the full (key, id) order).
+                const uint32_t mpar = qt_iter & 1;
+                if (half == 1) {
+                    ok = mbar_wait(&merge_empty[mt], mpar ^ 1, abort_flag);
+                    if (!ok) break;
+                    tk.for_each(p.k, [&](int jj, int32_t key, uint32_t id) {
+                        merge_slot[jj] = key;
+                        merge_slot[kCap + jj] = static_cast<int32_t>(id);
+                    });
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&merge_full[mt]);
+                    continue;
+                }
+                ok = mbar_wait(&merge_full[mt], mpar, abort_flag);
+                if (!ok) break;
+                for (uint32_t jj = 0; jj < p.k; ++jj) {
+                    const int32_t key = merge_slot[jj];
+                    const uint32_t id = static_cast<uint32_t>(merge_slot[kCap + jj]);
+                    if (key_gt(tk.thr(), tk.thr_id(), key, id)) tk.insert(key, id);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&merge_empty[mt]);
+            }
             if (!qvalid) continue;
             uint32_t* oid = p.out_ids + static_cast<uint64_t>(qlocal) * p.k;
             if constexpr (Elem::kFloat) {
@@ -494,6 +648,10 @@ __global__ void __launch_bounds__(64 + 128 * MT, 1)
                     p.fallback_rows[slot] = qlocal;
                 }
             }
+        }
+        if (dbg) {
+            atomicAdd(p.debug_clocks + 3, static_cast<unsigned long long>(c_tfull));
+            atomicAdd(p.debug_clocks + 4, static_cast<unsigned long long>(clock64() - c_start));
         }
         if (!ok) {
             atomicOr(p.error, 4);

@@ -181,24 +181,25 @@ struct TcMaps {
     CUtensorMap q0, q1, b0, b1;
 };
 
-template <class Elem, int MT, int NBUF, bool A_STREAM, int METRIC, class TopK>
+template <class Elem, int MT, int NBUF, bool A_STREAM, int METRIC, class TopK, int SPLIT = 1>
 knng_gpu_status launch_tc_t(const TcMaps& m, const KnnTcParams& p, cudaStream_t st)
 {
-    const SmemLayoutTc L = smem_layout_tc(Elem::kPlanes, MT, A_STREAM, p.kchunks, p.stages);
+    const SmemLayoutTc L =
+        smem_layout_tc(Elem::kPlanes, MT, A_STREAM, p.kchunks, p.stages, SPLIT, SPLIT > 1 ? TopK::kRegs / 2 : 0);
     const uint32_t smem = L.total + 1024;
-    auto kern = knn_tc_kernel<Elem, MT, NBUF, A_STREAM, METRIC, TopK>;
+    auto kern = knn_tc_kernel<Elem, MT, NBUF, A_STREAM, METRIC, TopK, SPLIT>;
     KNNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const uint32_t n_qtiles = (p.n_queries + MT * kTileRows - 1) / (MT * kTileRows);
     const uint32_t grid = std::min<uint32_t>(n_qtiles, static_cast<uint32_t>(sm_count()));
-    kern<<<grid, 64 + 128 * MT, smem, st>>>(m.q0, m.q1, m.b0, m.b1, p);
+    kern<<<grid, 64 + 128 * MT * SPLIT, smem, st>>>(m.q0, m.q1, m.b0, m.b1, p);
     KNNG_CUDA(cudaGetLastError());
     return KNNG_GPU_OK;
 }
 
 // Stages that fit the shared-memory budget for a tile configuration.
-uint32_t pick_stages(int planes, int mt, bool a_stream, uint32_t kchunks)
+uint32_t pick_stages(int planes, int mt, bool a_stream, uint32_t kchunks, int split = 1, int kcap = 0)
 {
-    const SmemLayoutTc L0 = smem_layout_tc(planes, mt, a_stream, kchunks, 0);
+    const SmemLayoutTc L0 = smem_layout_tc(planes, mt, a_stream, kchunks, 0, split, kcap);
     const uint32_t budget = 227u * 1024u - 1024u;
     if (L0.total >= budget) return 0;
     uint32_t s = std::min<uint32_t>(16, (budget - L0.total) / L0.stage_bytes);
@@ -207,8 +208,12 @@ uint32_t pick_stages(int planes, int mt, bool a_stream, uint32_t kchunks)
 }
 
 template <int MT, int METRIC>
-knng_gpu_status launch_u8_k(const TcMaps& m, const KnnTcParams& p, cudaStream_t st)
+knng_gpu_status launch_u8_k(const TcMaps& m, const KnnTcParams& p, cudaStream_t st, int split)
 {
+    if constexpr (MT == 2) {
+        if (split == 2 && p.k <= 10) return launch_tc_t<ElemU8, MT, 2, false, METRIC, RegTopK<10>, 2>(m, p, st);
+        if (split == 2 && p.k <= 16) return launch_tc_t<ElemU8, MT, 2, false, METRIC, RegTopK<16>, 2>(m, p, st);
+    }
     if (p.k <= 10) return launch_tc_t<ElemU8, MT, 2, false, METRIC, RegTopK<10>>(m, p, st);
     if (p.k <= 16) return launch_tc_t<ElemU8, MT, 2, false, METRIC, RegTopK<16>>(m, p, st);
     if (p.k <= 32) return launch_tc_t<ElemU8, MT, 2, false, METRIC, RegTopK<32>>(m, p, st);
@@ -369,15 +374,41 @@ knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int me
         if (const char* dbg = std::getenv("KNNG_GPU_DEBUG_FLAGS")) p.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
         // Two query tiles per CTA need k <= 32 (register budget of 320 threads).
         const int mt = (p.kchunks <= 2 && k <= 32) ? 2 : 1;
-        p.stages = pick_stages(1, mt, false, p.kchunks);
+        // Optional column-split epilogue (four epilogue warps per SM
+        // sub-partition, each on half of a 256-column tile), KNNG_GPU_SPLIT=2.
+        // Measured slower than one warp per 32 rows at n=1M d=128 k=10 on B200
+        // (305 ms vs 263 ms: the 96-register budget spills), so off by default.
+        int split = 1;
+        if (const char* sv = std::getenv("KNNG_GPU_SPLIT")) split = (std::atoi(sv) == 2 && mt == 2 && k <= 16) ? 2 : 1;
+        p.stages = pick_stages(1, mt, false, p.kchunks, split, split > 1 ? (k <= 10 ? 10 : 16) : 0);
+        if (split > 1 && p.stages < 3) {
+            split = 1;
+            p.stages = pick_stages(1, mt, false, p.kchunks);
+        }
         if (p.stages < 2 || (mt > 1 && p.stages < p.kchunks))
             return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: shared memory budget exceeded");
+        unsigned long long* dbg_clk = nullptr;
+        if (p.debug_flags & 512u) {  // profiling only
+            cudaMalloc(&dbg_clk, 8 * sizeof(unsigned long long));
+            cudaMemsetAsync(dbg_clk, 0, 8 * sizeof(unsigned long long), st);
+            p.debug_clocks = dbg_clk;
+        }
         knng_gpu_status s;
         if (mt == 2)
-            s = metric == 0 ? launch_u8_k<2, 0>(m, p, st) : launch_u8_k<2, 1>(m, p, st);
+            s = metric == 0 ? launch_u8_k<2, 0>(m, p, st, split) : launch_u8_k<2, 1>(m, p, st, split);
         else
-            s = metric == 0 ? launch_u8_k<1, 0>(m, p, st) : launch_u8_k<1, 1>(m, p, st);
+            s = metric == 0 ? launch_u8_k<1, 0>(m, p, st, split) : launch_u8_k<1, 1>(m, p, st, split);
         KNNG_TRY(s);
+        if (dbg_clk) {
+            unsigned long long h[8];
+            cudaMemcpyAsync(h, dbg_clk, sizeof(h), cudaMemcpyDeviceToHost, st);
+            cudaStreamSynchronize(st);
+            std::fprintf(stderr,
+                         "knng debug clocks (sum over CTAs): mma wait_tempty %llu wait_full %llu total %llu | "
+                         "epi0 wait_tfull %llu total %llu | producer wait_stage %llu total %llu\n",
+                         h[0], h[1], h[2], h[3], h[4], h[5], h[6]);
+            cudaFree(dbg_clk);
+        }
         tk.stop(st);
         // Rows whose fp32 sums may round: recompute exactly (device-side
         // count; CTAs past it exit at once).

@@ -114,6 +114,21 @@ __device__ __forceinline__ bool spin_until_geq(volatile uint32_t* counter, uint3
     }
 }
 
+// ---------------------------------------------------------------- cp.async
+// 16-byte global -> shared copy; bytes past src_bytes are zero-filled.
+__device__ __forceinline__ void cp_async_16_zfill(void* smem_dst, const void* gsrc, uint32_t src_bytes)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
+                 "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y,
                                             uint64_t* bar)
