@@ -43,6 +43,8 @@ constexpr int kSlowPitch = 36;      // ints per thread in the slow-path spill ar
 constexpr int kNormRing = 4;        // base-tile norm slots per epilogue warp (prefetch depth + 1)
 // Software-pipelined TMEM loads in the epilogue (measured slower at d = 128).
 constexpr bool kPipelineTmemLoads = false;
+// Small lists: load a whole tile before handing the TMEM buffer back.
+constexpr bool kLoadWholeTile = false;
 
 struct ElemU8 {
     static constexpr int kPlanes = 1;
@@ -229,9 +231,10 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
         if (lane == 0) {
             const CUtensorMap* qmap[2] = {&tmap_q0, &tmap_q1};
             const CUtensorMap* bmap[2] = {&tmap_b0, &tmap_b1};
-            uint32_t stage = 0, phase = 0, a_par = 0, load_idx = 0;
+            uint32_t stage = 0, phase = 0, a_par = 0, load_idx = 0, rel_tile = 0, rel_kc = 0;
             bool ok = true;
             const bool dbg = (p.debug_flags & 512u) && p.debug_clocks;
+            const bool no_tma = (p.debug_flags & 2048u) != 0;  // profiling only
             long long c_wait = 0, c_start = clock64();
             for (uint32_t t = blockIdx.x; t < n_qtiles && ok; t += gridDim.x) {
                 if (!A_STREAM) {
@@ -252,19 +255,34 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                             ok = mbar_wait(&empty[stage], phase ^ 1, abort_flag);
                             if (!ok) break;
                         } else if (load_idx >= S) {
-                            // The stage last held load (load_idx - S), part of
-                            // tile (load_idx - S) / kchunks.
-                            const long long w0 = clock64();
-                            ok = spin_until_geq(tiles_done, (load_idx - S) / p.kchunks + 1, abort_flag);
-                            c_wait += clock64() - w0;
+                            // The stage last held load (load_idx - S), chunk
+                            // rel_kc of tile rel_tile (counted incrementally:
+                            // no division in this single-thread loop).
+                            if (dbg) {
+                                const long long w0 = clock64();
+                                ok = spin_until_geq(tiles_done, rel_tile + 1, abort_flag, 256);
+                                c_wait += clock64() - w0;
+                            } else {
+                                ok = spin_until_geq(tiles_done, rel_tile + 1, abort_flag, 256);
+                            }
                             if (!ok) break;
+                            if (++rel_kc == p.kchunks) {
+                                rel_kc = 0;
+                                ++rel_tile;
+                            }
                         }
                         ++load_idx;
-                        mbar_arrive_expect_tx(&full[stage], stage_bytes);
+                        if (no_tma) {  // profiling: stage handoff without data
+                            mbar_arrive(&full[stage]);
+                        } else {
+                            mbar_arrive_expect_tx(&full[stage], stage_bytes);
+                        }
                         const int32_t x = kc * kChunkBytes / (Elem::kFloat ? 2 : 1);
                         uint8_t* dst = sB + stage * stage_bytes;
-                        for (int pl = 0; pl < P; ++pl) tma_load_2d(dst + pl * kBoxBytes, bmap[pl], x, j * BN, &full[stage]);
-                        if (A_STREAM) {
+                        if (!no_tma)
+                            for (int pl = 0; pl < P; ++pl)
+                                tma_load_2d(dst + pl * kBoxBytes, bmap[pl], x, j * BN, &full[stage]);
+                        if (A_STREAM && !no_tma) {
                             for (int mt = 0; mt < MT; ++mt)
                                 for (int pl = 0; pl < P; ++pl)
                                     tma_load_2d(dst + ((1 + mt) * P + pl) * kBoxBytes, qmap[pl], x,
@@ -302,6 +320,11 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
             bool ok = true;
             const bool dbg = (p.debug_flags & 512u) && p.debug_clocks;
             const bool no_mma = (p.debug_flags & 128u) != 0;  // profiling: epilogue without MMAs
+            // profiling only: 64 = do not wait for the TMEM handoff (idle
+            // epilogue), 32 = one extra commit per tile
+            const bool skip_tempty = (p.debug_flags & 64u) != 0, extra_commit = (p.debug_flags & 32u) != 0;
+            const bool lean = !Elem::kFloat && !A_STREAM && NBUF == 2 && !kPerMtBars && p.kchunks == 1 &&
+                              !stage_commits && (p.debug_flags & (64u | 32u | 128u | 512u | 4096u)) == 0;
             long long c_tempty = 0, c_full = 0, c_start = clock64();
             // Issue the K steps of one 128-byte K chunk for M tile mt.
             auto issue_chunk = [&](uint32_t d_tmem, int mt, uint32_t kc, uint32_t stage, bool first) {
@@ -312,9 +335,11 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                                      : a_desc0 + ((mt * p.kchunks + kc) * P + pl) * kBoxStep;
                     b[pl] = b_desc0 + stage * stage_step + pl * kBoxStep;
                 }
+                // Straight-line MMAs: no branch between them (control flow
+                // around each tcgen05.mma costs the issuing thread dearly).
 #pragma unroll
                 for (int ks = 0; ks < kChunkBytes / 32; ++ks) {
-                    if (!no_mma) Elem::mma_step(d_tmem, a, b, idesc, (first && ks == 0) ? 0u : 1u);
+                    Elem::mma_step(d_tmem, a, b, idesc, (first && ks == 0) ? 0u : 1u);
 #pragma unroll
                     for (int pl = 0; pl < P; ++pl) {
                         a[pl] += 2;  // 32 bytes
@@ -329,7 +354,34 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                     a_par ^= 1;
                     tc_fence_after();
                 }
-                for (uint32_t j = 0; j < n_btiles && ok; ++j, ++acc_i) {
+                if constexpr (!Elem::kFloat && !A_STREAM && NBUF == 2 && !kPerMtBars) if (lean) {
+                    // Hot configuration (one K chunk, resident A, two TMEM
+                    // buffers, stages released by counter): per tile two waits,
+                    // one fence, the MMAs as straight-line code, one commit.
+                    for (uint32_t j = 0; j < n_btiles; ++j, ++acc_i) {
+                        const uint32_t buf = acc_i & 1u;
+                        if (!mbar_wait_sleep(&tempty[buf], ((acc_i >> 1) & 1u) ^ 1u, abort_flag) ||
+                            !mbar_wait_sleep(&full[s], ph, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint64_t bd = b_desc0 + s * stage_step;
+                        const uint32_t d0 = tmem_base + buf * (MT * BN);
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                            for (int ks = 0; ks < kChunkBytes / 32; ++ks)
+                                umma_u8(d0 + mt * BN, a_desc0 + mt * kBoxStep + 2 * ks, bd + 2 * ks, idesc,
+                                        ks > 0 ? 1u : 0u);
+                        if (++s == S) {
+                            s = 0;
+                            ph ^= 1;
+                        }
+                        umma_commit(&tfull[buf]);
+                    }
+                }
+                for (uint32_t j = 0; !lean && j < n_btiles && ok; ++j, ++acc_i) {
                     const uint32_t buf = NBUF == 1 ? 0u : acc_i & (NBUF - 1);
                     const uint32_t tpar = (acc_i / NBUF) & 1;
                     if (kPerMtBars) {
@@ -364,29 +416,40 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                                     if (!ok) break;
                                     tc_fence_after();
                                 }
-                                issue_chunk(tmem_base + mt * BN, mt, kc, st_k[kc], kc == 0);
+                                if (!no_mma) issue_chunk(tmem_base + mt * BN, mt, kc, st_k[kc], kc == 0);
                                 if (stage_commits && mt == MT - 1) umma_commit(&empty[st_k[kc]]);
                             }
                             if (ok) umma_commit(&tfull[mt]);
                         }
                     } else {
-                        // debug 64 (profiling with an idle epilogue only): do not wait for the handoff
-                        if (!(p.debug_flags & 64u)) {
-                            const long long w0 = clock64();
-                            ok = mbar_wait(&tempty[buf], tpar ^ 1, abort_flag);
-                            c_tempty += clock64() - w0;
+                        // Both waits first, then one fence for the MMAs that
+                        // follow. Clock reads only when profiling: every extra
+                        // instruction in this thread delays the next MMAs.
+                        if (!skip_tempty) {
+                            if (dbg) {
+                                const long long w0 = clock64();
+                                ok = mbar_wait(&tempty[buf], tpar ^ 1, abort_flag);
+                                c_tempty += clock64() - w0;
+                            } else {
+                                ok = mbar_wait(&tempty[buf], tpar ^ 1, abort_flag);
+                            }
                             if (!ok) break;
                         }
-                        tc_fence_after();
                         for (uint32_t kc = 0; kc < p.kchunks && ok; ++kc) {
-                            const long long w1 = clock64();
-                            ok = mbar_wait(&full[s], ph, abort_flag);
-                            c_full += clock64() - w1;
+                            if (dbg) {
+                                const long long w1 = clock64();
+                                ok = mbar_wait(&full[s], ph, abort_flag);
+                                c_full += clock64() - w1;
+                            } else {
+                                ok = mbar_wait(&full[s], ph, abort_flag);
+                            }
                             if (!ok) break;
                             tc_fence_after();
+                            if (!no_mma) {
 #pragma unroll
-                            for (int mt = 0; mt < MT; ++mt)
-                                issue_chunk(tmem_base + (buf * MT + mt) * BN, mt, kc, s, kc == 0);
+                                for (int mt = 0; mt < MT; ++mt)
+                                    issue_chunk(tmem_base + (buf * MT + mt) * BN, mt, kc, s, kc == 0);
+                            }
                             if (stage_commits) umma_commit(&empty[s]);
                             if (++s == S) {
                                 s = 0;
@@ -394,7 +457,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                             }
                         }
                         if (ok) umma_commit(&tfull[buf]);
-                        if (p.debug_flags & 32u) umma_commit(&bars[60]);  // profiling: one extra commit per tile
+                        if (extra_commit) umma_commit(&bars[60]);  // profiling: one extra commit per tile
                     }
                 }
                 if (ok && !A_STREAM) umma_commit(a_empty);
@@ -571,6 +634,22 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                             __syncwarp();
                             if (loads) tmem_ld_wait_n<32>(vn);
                         }
+                    }
+                } else if constexpr (kLoadWholeTile && SPLIT == 1 && TopK::kRegs <= 32) {
+                    // Small lists: the whole 128-column tile into registers,
+                    // the buffer handed back at once (the TMEM round trip is
+                    // the throughput limit), then filtered in two halves.
+                    int32_t v[kCols];
+                    __syncwarp();
+                    if (loads) {
+#pragma unroll
+                        for (int c = 0; c < kCols / 32; ++c) tmem_ld_32cols(tb + c * 32, v + c * 32);
+                        tmem_ld_wait_n<kCols>(v);
+                    }
+                    release();
+                    if (filtering) {
+                        filter(v, std::integral_constant<int, kCols / 2>{}, 0);
+                        filter(v + kCols / 2, std::integral_constant<int, kCols / 2>{}, kCols / 2);
                     }
                 } else {
                     // Larger lists: steps of kW columns, one TMEM wait per step.

@@ -190,7 +190,8 @@ knng_gpu_status launch_tc_t(const TcMaps& m, const KnnTcParams& p, cudaStream_t 
     auto kern = knn_tc_kernel<Elem, MT, NBUF, A_STREAM, METRIC, TopK, SPLIT>;
     KNNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const uint32_t n_qtiles = (p.n_queries + MT * kTileRows - 1) / (MT * kTileRows);
-    const uint32_t grid = std::min<uint32_t>(n_qtiles, static_cast<uint32_t>(sm_count()));
+    uint32_t grid = std::min<uint32_t>(n_qtiles, static_cast<uint32_t>(sm_count()));
+    if (const char* gv = std::getenv("KNNG_GPU_GRID")) grid = std::min<uint32_t>(grid, std::max(1, std::atoi(gv)));  // experiments only
     kern<<<grid, 64 + 128 * MT * SPLIT, smem, st>>>(m.q0, m.q1, m.b0, m.b1, p);
     KNNG_CUDA(cudaGetLastError());
     return KNNG_GPU_OK;
@@ -373,7 +374,8 @@ knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int me
         p.error = reinterpret_cast<int*>(sc.counters + 1);
         if (const char* dbg = std::getenv("KNNG_GPU_DEBUG_FLAGS")) p.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
         // Two query tiles per CTA need k <= 32 (register budget of 320 threads).
-        const int mt = (p.kchunks <= 2 && k <= 32) ? 2 : 1;
+        int mt = (p.kchunks <= 2 && k <= 32) ? 2 : 1;
+        if (const char* mv = std::getenv("KNNG_GPU_MT")) mt = std::atoi(mv) == 1 ? 1 : mt;  // experiments only
         // Optional column-split epilogue (four epilogue warps per SM
         // sub-partition, each on half of a 256-column tile), KNNG_GPU_SPLIT=2.
         // Measured slower than one warp per 32 rows at n=1M d=128 k=10 on B200

@@ -56,6 +56,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in the barrier until
+// the phase completes or ~`ns` pass, issuing nothing meanwhile (single-thread
+// roles that share an SM sub-partition with busy warps).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity)
 {
     uint32_t ok;
@@ -99,8 +115,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// mbar_wait for the single-thread roles: suspended in the barrier between
+// polls (hint ~0.1 ms), so a waiting producer / MMA thread takes no issue slots.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort)
+{
+    if (mbar_try_wait_hint(bar, parity, 100000u)) return true;
+    const long long t0 = clock64();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait_hint(bar, parity, 100000u)) return true;
+        if ((it & 15u) == 0) {
+            if (*abort) return false;
+            if (clock64() - t0 > kSpinLimitCycles) return false;
+        }
+    }
+}
+
 // Bounded wait until a shared-memory counter reaches `target`.
-__device__ __forceinline__ bool spin_until_geq(volatile uint32_t* counter, uint32_t target, volatile int* abort)
+__device__ __forceinline__ bool spin_until_geq(volatile uint32_t* counter, uint32_t target, volatile int* abort,
+                                               uint32_t sleep_ns = 32)
 {
     if (*counter >= target) return true;
     const long long t0 = clock64();
@@ -110,7 +142,7 @@ __device__ __forceinline__ bool spin_until_geq(volatile uint32_t* counter, uint3
             if (*abort) return false;
             if (clock64() - t0 > kSpinLimitCycles) return false;
         }
-        __nanosleep(32);
+        __nanosleep(sleep_ns);
     }
 }
 
