@@ -237,7 +237,7 @@ def main() -> None:
     builder.build(x_slice)
     phases = builder.phase_ms()
     builder.timing = False
-    launches_per_step = int(builder.last_stats.get("kernel_launches", 0)) + 1  # + pack
+    launches_per_step = int(builder.last_stats.get("kernel_launches", 0)) + 2  # + pack and augmentation
     t = torch.tensor([step_ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

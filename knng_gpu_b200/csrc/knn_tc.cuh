@@ -39,6 +39,8 @@ namespace knng_b200 {
 constexpr int kTileRows = 128;      // M per UMMA, N per base tile, rows per TMA box
 constexpr int kChunkBytes = 128;    // K bytes per TMA box / swizzle atom
 constexpr int kBoxBytes = kTileRows * kChunkBytes;  // 16 KiB
+constexpr int kAugBytes = 32;       // augmentation K bytes per packed u8 row (after the data)
+constexpr int kAugBox = kTileRows * kAugBytes;  // 4 KiB: one tile of augmentation bytes
 constexpr int kSlowPitch = 36;      // ints per thread in the slow-path spill area
 constexpr int kNormRing = 4;        // base-tile norm slots per epilogue warp (prefetch depth + 1)
 // Software-pipelined TMEM loads in the epilogue (measured slower at d = 128).
@@ -72,8 +74,13 @@ struct ElemBf16x3 {
 };
 
 struct KnnTcParams {
-    const void* base_norms;      // per base row: int32 |r|^2 (u8 L2) or fp32 |r'|^2 (bf16x3 L2)
-    const int32_t* query_norms;  // u8 L2: |q|^2 per query row of this launch
+    const void* base_norms;      // per base row: int32 key offset (u8 L2) or fp32 |r'|^2 (bf16x3 L2)
+    const int32_t* query_norms;  // u8: key offset per query row of this launch (see below)
+    // u8: packed query rows (augmentation bytes at data_bytes within each
+    // pitch-byte row); L2 recovers |q|^2 = keyoff - 510 * sum(aug bytes).
+    const uint8_t* query_packed;
+    uint32_t pitch;
+    uint32_t data_bytes;
     uint64_t n_base;             // valid base rows
     uint32_t base_id0;           // global id of base row 0
     uint32_t n_queries;          // query rows in this launch
@@ -94,22 +101,25 @@ struct KnnTcParams {
 };
 
 struct SmemLayoutTc {
-    uint32_t a_off, b_off, nb_off, slow_off, merge_off, bar_off, total, stage_bytes, a_bytes;
+    uint32_t a_off, aug_off, b_off, nb_off, slow_off, merge_off, bar_off, total, stage_bytes, a_bytes;
 };
 
 // split: epilogue warps per (M tile, TMEM lane quarter), each covering
 // 1/split of the columns; their lists meet in `merge` (2 * kcap ints per row).
+// aug: u8 L2 -- a constant 4 KiB block of query-side augmentation bytes
+// after A, and 4 KiB of base-side augmentation bytes in every stage.
 __host__ __device__ inline SmemLayoutTc smem_layout_tc(int planes, int mt, bool a_stream, uint32_t kchunks,
-                                                       uint32_t stages, int split = 1, int kcap = 0)
+                                                       uint32_t stages, int split = 1, int kcap = 0, bool aug = false)
 {
     SmemLayoutTc L;
     // A resident: all K chunks of MT tiles. A streamed: a stage carries the
     // A chunk(s) next to the B chunk.
     L.a_bytes = a_stream ? 0 : mt * kchunks * planes * kBoxBytes;
-    L.stage_bytes = (a_stream ? mt + 1 : 1) * planes * kBoxBytes;
+    L.stage_bytes = (a_stream ? mt + 1 : 1) * planes * kBoxBytes + (aug ? kAugBox : 0);
     const int epi_threads = mt * kTileRows * split;
     L.a_off = 0;
-    L.b_off = L.a_off + L.a_bytes;
+    L.aug_off = L.a_off + L.a_bytes;
+    L.b_off = L.aug_off + (aug ? kAugBox : 0);
     L.nb_off = L.b_off + stages * L.stage_bytes;
     L.slow_off = L.nb_off + (epi_threads / 32) * kNormRing * kTileRows * 4;  // per epilogue warp ring
     L.merge_off = L.slow_off + epi_threads * kSlowPitch * 4;
@@ -132,6 +142,21 @@ __device__ __forceinline__ int32_t tree_min(const int32_t* v)
     } else {
         constexpr int a = N / 3, b = (N - a) / 2, c = N - a - b;
         return __vimin3_s32(tree_min<a>(v), tree_min<b>(v + a), tree_min<c>(v + a + b));
+    }
+}
+
+template <int N>
+__device__ __forceinline__ int32_t tree_max(const int32_t* v)
+{
+    if constexpr (N == 1) {
+        return v[0];
+    } else if constexpr (N == 2) {
+        return max(v[0], v[1]);
+    } else if constexpr (N == 3) {
+        return __vimax3_s32(v[0], v[1], v[2]);
+    } else {
+        constexpr int a = N / 3, b = (N - a) / 2, c = N - a - b;
+        return __vimax3_s32(tree_max<a>(v), tree_max<b>(v + a), tree_max<c>(v + a + b));
     }
 }
 
@@ -161,8 +186,13 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const SmemLayoutTc L = smem_layout_tc(P, MT, A_STREAM, p.kchunks, p.stages, SPLIT, SPLIT > 1 ? kCap : 0);
+    // u8 L2: the K dimension is extended by 32 bytes so that the accumulator
+    // already holds q.r + 255 * S(r); the key is keyoff(r) - 2 * acc with
+    // keyoff(r) = |r|^2 + 510 * S(r), and the filter needs only a maximum.
+    constexpr bool kAug = !Elem::kFloat && METRIC == 0;
+    const SmemLayoutTc L = smem_layout_tc(P, MT, A_STREAM, p.kchunks, p.stages, SPLIT, SPLIT > 1 ? kCap : 0, kAug);
     uint8_t* sA = smem + L.a_off;
+    uint8_t* sAaug = smem + L.aug_off;
     uint8_t* sB = smem + L.b_off;
     int32_t* sNB = reinterpret_cast<int32_t*>(smem + L.nb_off);
     int32_t* sSlow = reinterpret_cast<int32_t*>(smem + L.slow_off);
@@ -220,6 +250,13 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
             prefetch_tensormap(&tmap_b1);
         }
     }
+    if constexpr (kAug) {
+        // Query-side augmentation bytes: 255 in every position (so the
+        // swizzle of the 32-byte rows is immaterial).
+        for (uint32_t i = threadIdx.x; i < kAugBox / 16; i += blockDim.x)
+            reinterpret_cast<uint4*>(sAaug)[i] = make_uint4(~0u, ~0u, ~0u, ~0u);
+        fence_proxy_async_smem();
+    }
     if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
     tc_fence_before();
     __syncthreads();
@@ -272,16 +309,20 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                             }
                         }
                         ++load_idx;
+                        // The augmentation tile rides with the last K chunk.
+                        const bool aug_here = kAug && kc + 1 == p.kchunks;
                         if (no_tma) {  // profiling: stage handoff without data
                             mbar_arrive(&full[stage]);
                         } else {
-                            mbar_arrive_expect_tx(&full[stage], stage_bytes);
+                            mbar_arrive_expect_tx(&full[stage], stage_bytes - ((kAug && !aug_here) ? kAugBox : 0));
                         }
                         const int32_t x = kc * kChunkBytes / (Elem::kFloat ? 2 : 1);
                         uint8_t* dst = sB + stage * stage_bytes;
-                        if (!no_tma)
+                        if (!no_tma) {
                             for (int pl = 0; pl < P; ++pl)
                                 tma_load_2d(dst + pl * kBoxBytes, bmap[pl], x, j * BN, &full[stage]);
+                            if (aug_here) tma_load_2d(dst + kBoxBytes, &tmap_b1, 0, j * BN, &full[stage]);
+                        }
                         if (A_STREAM && !no_tma) {
                             for (int mt = 0; mt < MT; ++mt)
                                 for (int pl = 0; pl < P; ++pl)
@@ -314,6 +355,9 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
             const uint32_t idesc = Elem::idesc();
             const uint64_t a_desc0 = umma_desc_sw128(smem_u32(sA));
             const uint64_t b_desc0 = umma_desc_sw128(smem_u32(sB));
+            // u8 L2: augmentation operands (32-byte swizzled rows)
+            const uint64_t a_aug_desc = umma_desc_sw32(smem_u32(sAaug));
+            const uint64_t b_aug_desc0 = umma_desc_sw32(smem_u32(sB + kBoxBytes));
             constexpr uint64_t kBoxStep = kBoxBytes >> 4;  // descriptor units per 16 KiB box
             const uint64_t stage_step = stage_bytes >> 4;
             uint32_t s = 0, ph = 0, a_par = 0, acc_i = 0;
@@ -346,6 +390,9 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                         b[pl] += 2;
                     }
                 }
+                if constexpr (kAug) {
+                    if (kc + 1 == p.kchunks) umma_u8(d_tmem, a_aug_desc, b_aug_desc0 + stage * stage_step, idesc, 1u);
+                }
             };
             for (uint32_t t = blockIdx.x; t < n_qtiles && ok; t += gridDim.x) {
                 if (!A_STREAM) {
@@ -368,12 +415,15 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                         tc_fence_after();
                         const uint64_t bd = b_desc0 + s * stage_step;
                         const uint32_t d0 = tmem_base + buf * (MT * BN);
+                        const uint64_t bd_aug = b_aug_desc0 + s * stage_step;
 #pragma unroll
-                        for (int mt = 0; mt < MT; ++mt)
+                        for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
                             for (int ks = 0; ks < kChunkBytes / 32; ++ks)
                                 umma_u8(d0 + mt * BN, a_desc0 + mt * kBoxStep + 2 * ks, bd + 2 * ks, idesc,
                                         ks > 0 ? 1u : 0u);
+                            if constexpr (kAug) umma_u8(d0 + mt * BN, a_aug_desc, bd_aug, idesc, 1u);
+                        }
                         if (++s == S) {
                             s = 0;
                             ph ^= 1;
@@ -528,10 +578,39 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
             const uint32_t qlocal = (t * MT + mt) * kTileRows + row;
             const bool qvalid = qlocal < p.n_queries;
             const uint32_t self_id = p.exclude_self ? p.query_id0 + qlocal : UINT32_MAX;
-            const int32_t qnorm = (!Elem::kFloat && METRIC == 0 && qvalid) ? p.query_norms[qlocal] : 0;
+            int32_t qnorm = 0;
+            if constexpr (kAug) {
+                if (qvalid) {
+                    // |q|^2 = keyoff(q) - 510 * (sum of q's augmentation bytes)
+                    const uint4* a4 = reinterpret_cast<const uint4*>(p.query_packed + static_cast<uint64_t>(qlocal) * p.pitch +
+                                                                     p.data_bytes);
+                    const uint4 w0 = a4[0], w1 = a4[1];
+                    uint32_t sb = 0;
+                    sb = __dp4a(w0.x, 0x01010101u, sb);
+                    sb = __dp4a(w0.y, 0x01010101u, sb);
+                    sb = __dp4a(w0.z, 0x01010101u, sb);
+                    sb = __dp4a(w0.w, 0x01010101u, sb);
+                    sb = __dp4a(w1.x, 0x01010101u, sb);
+                    sb = __dp4a(w1.y, 0x01010101u, sb);
+                    sb = __dp4a(w1.z, 0x01010101u, sb);
+                    sb = __dp4a(w1.w, 0x01010101u, sb);
+                    qnorm = p.query_norms[qlocal] - 510 * static_cast<int32_t>(sb);
+                }
+            }
             TopK tk;
             tk.init(p.k);
             int32_t thr = tk.thr();
+            // u8: a column can enter the list only if its accumulator exceeds
+            // lim (keys are keyoff - 2 acc >= keyoff_min(tile) - 2 acc for L2,
+            // -acc for IP); recomputed per tile and after every insertion.
+            int32_t hmin = 0, lim = 0;
+            auto lim_of = [&](int32_t t) -> int32_t {
+                if constexpr (METRIC == 0) {
+                    return static_cast<int32_t>((static_cast<long long>(hmin) - t) >> 1);  // floor
+                } else {
+                    return -t;
+                }
+            };
             __syncwarp();
             for (uint32_t jj = 0; jj + 1 < kNormRing; ++jj) {
                 if (jj < n_btiles) fetch_norms(jj);
@@ -559,45 +638,73 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                                     half * (BN / SPLIT);
                 constexpr int kCols = BN / SPLIT;  // columns of each tile this thread filters
                 const int4* nb4 = reinterpret_cast<const int4*>(nbuf + (j % kNormRing) * BN + half * kCols);
-                // Keys of W columns (starting at column c0 of the tile), one
-                // threshold test on their minimum, and the rare insertion path:
-                // spill the keys and insert those under the running threshold,
-                // in id order.
-                auto filter = [&](int32_t* v, auto w_tag, int c0) {
+                if constexpr (!Elem::kFloat) {
+                    if constexpr (METRIC == 0) {
+                        // Smallest key offset of the tile (padding columns
+                        // hold INT_MAX): one 16-byte read per lane + a reduce.
+                        const int4 h4 = reinterpret_cast<const int4*>(nbuf + (j % kNormRing) * BN)[lane];
+                        hmin = __reduce_min_sync(0xffffffffu, min(min(h4.x, h4.y), min(h4.z, h4.w)));
+                    }
+                    lim = lim_of(thr);
+                }
+                // Insertion path for W columns starting at column c0 of the
+                // tile, whose keys are in v: spill them and insert those under
+                // the running threshold, in id order.
+                auto insert_keys = [&](const int32_t* v, auto w_tag, int c0) {
                     constexpr int W = decltype(w_tag)::value;
 #pragma unroll
-                    for (int i4 = 0; i4 < W / 4; ++i4) {
-                        const int4 nn = nb4[c0 / 4 + i4];
-                        v[4 * i4 + 0] = key_of(v[4 * i4 + 0], nn.x);
-                        v[4 * i4 + 1] = key_of(v[4 * i4 + 1], nn.y);
-                        v[4 * i4 + 2] = key_of(v[4 * i4 + 2], nn.z);
-                        v[4 * i4 + 3] = key_of(v[4 * i4 + 3], nn.w);
-                    }
-                    const int32_t step_min = tree_min<W>(v);  // depth log3(W)
-                    if (step_min < thr && !(p.debug_flags & 2u)) {
+                    for (int c = 0; c < W / 32; ++c) {
+                        const int32_t* vc = v + c * 32;
+                        uint32_t mask = 0;
 #pragma unroll
-                        for (int c = 0; c < W / 32; ++c) {
-                            const int32_t* vc = v + c * 32;
-                            uint32_t mask = 0;
+                        for (int i = 0; i < 32; ++i) mask |= (vc[i] < thr ? 1u : 0u) << i;
+                        if (!mask) continue;
 #pragma unroll
-                            for (int i = 0; i < 32; ++i) mask |= (vc[i] < thr ? 1u : 0u) << i;
-                            if (!mask) continue;
-#pragma unroll
-                            for (int i4 = 0; i4 < 8; ++i4)
-                                *reinterpret_cast<int4*>(slow + 4 * i4) =
-                                    make_int4(vc[4 * i4], vc[4 * i4 + 1], vc[4 * i4 + 2], vc[4 * i4 + 3]);
-                            const uint32_t col0 = p.base_id0 + j * BN + half * kCols + c0 + c * 32;
-                            while (mask) {
-                                const int i = __ffs(mask) - 1;
-                                mask &= mask - 1;
-                                const int32_t key = slow[i];
-                                const uint32_t id = col0 + i;
-                                if (key < thr && id != self_id) {
-                                    tk.insert_increasing(key, id);
-                                    thr = tk.thr();
-                                }
+                        for (int i4 = 0; i4 < 8; ++i4)
+                            *reinterpret_cast<int4*>(slow + 4 * i4) =
+                                make_int4(vc[4 * i4], vc[4 * i4 + 1], vc[4 * i4 + 2], vc[4 * i4 + 3]);
+                        const uint32_t col0 = p.base_id0 + j * BN + half * kCols + c0 + c * 32;
+                        while (mask) {
+                            const int i = __ffs(mask) - 1;
+                            mask &= mask - 1;
+                            const int32_t key = slow[i];
+                            const uint32_t id = col0 + i;
+                            if (key < thr && id != self_id) {
+                                tk.insert_increasing(key, id);
+                                thr = tk.thr();
                             }
                         }
+                    }
+                };
+                // One threshold test per W columns (starting at column c0 of
+                // the tile). u8: on the raw accumulators (maximum against lim);
+                // bf16x3: on the keys (minimum against the threshold).
+                auto filter = [&](int32_t* v, auto w_tag, int c0) {
+                    constexpr int W = decltype(w_tag)::value;
+                    if constexpr (!Elem::kFloat) {
+                        if (tree_max<W>(v) > lim && !(p.debug_flags & 2u)) {
+#pragma unroll
+                            for (int i4 = 0; i4 < W / 4; ++i4) {
+                                const int4 nn = nb4[c0 / 4 + i4];
+                                v[4 * i4 + 0] = key_of(v[4 * i4 + 0], nn.x);
+                                v[4 * i4 + 1] = key_of(v[4 * i4 + 1], nn.y);
+                                v[4 * i4 + 2] = key_of(v[4 * i4 + 2], nn.z);
+                                v[4 * i4 + 3] = key_of(v[4 * i4 + 3], nn.w);
+                            }
+                            insert_keys(v, w_tag, c0);
+                            lim = lim_of(thr);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i4 = 0; i4 < W / 4; ++i4) {
+                            const int4 nn = nb4[c0 / 4 + i4];
+                            v[4 * i4 + 0] = key_of(v[4 * i4 + 0], nn.x);
+                            v[4 * i4 + 1] = key_of(v[4 * i4 + 1], nn.y);
+                            v[4 * i4 + 2] = key_of(v[4 * i4 + 2], nn.z);
+                            v[4 * i4 + 3] = key_of(v[4 * i4 + 3], nn.w);
+                        }
+                        const int32_t step_min = tree_min<W>(v);  // depth log3(W)
+                        if (step_min < thr && !(p.debug_flags & 2u)) insert_keys(v, w_tag, c0);
                     }
                 };
                 auto release = [&]() {

@@ -75,7 +75,7 @@ knng_gpu_status validate(uint64_t n, uint64_t d, uint64_t k, int metric)
 // and the exact int32 squared norm (compute_norms_squared,
 // src/cpu/distance.cpp:17-38, exact for such data).
 __global__ void __launch_bounds__(256) pack_u8_kernel(const float* __restrict__ x, uint64_t rows, uint32_t d,
-                                                      uint32_t pitch, uint8_t* __restrict__ packed,
+                                                      uint32_t data_bytes, uint32_t pitch, uint8_t* __restrict__ packed,
                                                       int32_t* __restrict__ norms, int32_t* nonint)
 {
     const uint32_t lane = threadIdx.x & 31;
@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(256) pack_u8_kernel(const float* __restrict__ 
     for (uint64_t r = warp0; r < rows; r += nwarps) {
         const float* xr = x + r * d;
         int32_t sum = 0;
-        for (uint32_t c0 = lane * 4; c0 < pitch; c0 += 128) {
+        for (uint32_t c0 = lane * 4; c0 < data_bytes; c0 += 128) {
             float v[4] = {0.f, 0.f, 0.f, 0.f};
             if (vec && c0 + 3 < d) {
                 const float4 f = __ldcs(reinterpret_cast<const float4*>(xr + c0));
@@ -115,6 +115,46 @@ __global__ void __launch_bounds__(256) pack_u8_kernel(const float* __restrict__ 
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(nonint, 1);
 }
 
+// Augmentation of the packed rows for the tensor-core L2 filter. For each
+// 128-row tile of this pack call, C = max over its rows of ceil(|r|^2 / 2)
+// and S(r) = min(8160, (C - ceil(|r|^2 / 2)) / 255); the row's 32
+// augmentation bytes hold S(r) as min(255, max(0, S - 255 j)), j = 0..31, so
+// that a query side of 32 bytes of 255 adds 255 * S(r) to q.r. The norm is
+// replaced by the key offset keyoff(r) = |r|^2 + 510 * S(r): then
+// |r|^2 - 2 q.r = keyoff(r) - 2 (q.r + 255 S(r)), and within a tile keyoff
+// varies by at most 509 unless the tile's norms spread over more than
+// 2 * 255 * 8160 (rows past that keep S = 8160; every key stays exact).
+__global__ void __launch_bounds__(128) pack_aug_kernel(uint64_t rows, uint32_t data_bytes, uint32_t pitch,
+                                                       uint8_t* __restrict__ packed, int32_t* __restrict__ norms)
+{
+    __shared__ int32_t s_max[4];
+    const uint64_t r = static_cast<uint64_t>(blockIdx.x) * 128 + threadIdx.x;
+    const bool valid = r < rows;
+    const int32_t nr = valid ? norms[r] : 0;
+    const int32_t half = static_cast<int32_t>((static_cast<uint32_t>(nr) + 1u) >> 1);
+    int32_t m = __reduce_max_sync(0xffffffffu, valid ? half : 0);
+    if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = max(max(s_max[0], s_max[1]), max(s_max[2], s_max[3]));
+    if (!valid) return;
+    const int32_t sv = min(8160, (m - half) / 255);
+    uint32_t w[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int32_t b = min(255, max(0, sv - 255 * (4 * q + e)));
+            word |= static_cast<uint32_t>(b) << (8 * e);
+        }
+        w[q] = word;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(packed + r * pitch + data_bytes);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    norms[r] = nr + 510 * sv;
+}
+
 // ------------------------------------------------------------------ TMA maps
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -135,23 +175,29 @@ knng_gpu_status get_encode_fn(EncodeTiledFn* out)
     return KNNG_GPU_OK;
 }
 
-// rows x pitch elements, box 128 rows x 128 bytes, 128-byte swizzle; rows
-// past the end read as zeros.
+// rows x width elements with a row stride of stride_bytes; box of 128 rows x
+// box_bytes (128 with 128-byte swizzle, or 32 with 32-byte swizzle); rows past
+// the end read as zeros.
 knng_gpu_status make_map(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void* base,
-                         uint64_t rows, uint64_t pitch_elems)
+                         uint64_t rows, uint64_t width_elems, uint64_t stride_bytes, uint32_t box_bytes = kChunkBytes)
 {
     EncodeTiledFn enc;
     KNNG_TRY(get_encode_fn(&enc));
-    const cuuint64_t dims[2] = {pitch_elems, rows};
-    const cuuint64_t strides[1] = {pitch_elems * elem_bytes};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kChunkBytes / elem_bytes), static_cast<cuuint32_t>(kTileRows)};
+    const cuuint64_t dims[2] = {width_elems, rows};
+    const cuuint64_t strides[1] = {stride_bytes};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_bytes / elem_bytes), static_cast<cuuint32_t>(kTileRows)};
     const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapSwizzle sw = box_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_128B;
     CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return fail(KNNG_GPU_CUDA_ERROR, "knng::gpu: cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
     return KNNG_GPU_OK;
 }
+
+// Packed u8 row: the data (d rounded up to 128 bytes), then kAugBytes of
+// augmentation.
+uint64_t u8_data_bytes(uint64_t d) { return align_up(d == 0 ? 1 : d, kChunkBytes); }
 
 int sm_count()
 {
@@ -184,8 +230,8 @@ struct TcMaps {
 template <class Elem, int MT, int NBUF, bool A_STREAM, int METRIC, class TopK, int SPLIT = 1>
 knng_gpu_status launch_tc_t(const TcMaps& m, const KnnTcParams& p, cudaStream_t st)
 {
-    const SmemLayoutTc L =
-        smem_layout_tc(Elem::kPlanes, MT, A_STREAM, p.kchunks, p.stages, SPLIT, SPLIT > 1 ? TopK::kRegs / 2 : 0);
+    const SmemLayoutTc L = smem_layout_tc(Elem::kPlanes, MT, A_STREAM, p.kchunks, p.stages, SPLIT,
+                                          SPLIT > 1 ? TopK::kRegs / 2 : 0, !Elem::kFloat && METRIC == 0);
     const uint32_t smem = L.total + 1024;
     auto kern = knn_tc_kernel<Elem, MT, NBUF, A_STREAM, METRIC, TopK, SPLIT>;
     KNNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -198,9 +244,10 @@ knng_gpu_status launch_tc_t(const TcMaps& m, const KnnTcParams& p, cudaStream_t 
 }
 
 // Stages that fit the shared-memory budget for a tile configuration.
-uint32_t pick_stages(int planes, int mt, bool a_stream, uint32_t kchunks, int split = 1, int kcap = 0)
+uint32_t pick_stages(int planes, int mt, bool a_stream, uint32_t kchunks, int split = 1, int kcap = 0,
+                     bool aug = false)
 {
-    const SmemLayoutTc L0 = smem_layout_tc(planes, mt, a_stream, kchunks, 0, split, kcap);
+    const SmemLayoutTc L0 = smem_layout_tc(planes, mt, a_stream, kchunks, 0, split, kcap, aug);
     const uint32_t budget = 227u * 1024u - 1024u;
     if (L0.total >= budget) return 0;
     uint32_t s = std::min<uint32_t>(16, (budget - L0.total) / L0.stage_bytes);
@@ -351,14 +398,23 @@ knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int me
     e.out_ids = ids;
     e.out_dists = dists;
     if (d <= kMaxTensorDim) {
+        const uint64_t data_bytes = u8_data_bytes(d);
         TcMaps m;
-        KNNG_TRY(make_map(&m.q0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.q_packed, q_count, pitch));
-        KNNG_TRY(make_map(&m.b0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.b_packed, z.n_b, pitch));
+        KNNG_TRY(make_map(&m.q0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.q_packed, q_count, data_bytes, pitch));
+        KNNG_TRY(make_map(&m.b0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.b_packed, z.n_b, data_bytes, pitch));
         m.q1 = m.q0;
-        m.b1 = m.b0;
+        // L2: the base rows' augmentation bytes (32-byte boxes after the data)
+        if (metric == 0)
+            KNNG_TRY(make_map(&m.b1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.b_packed + data_bytes, z.n_b, kAugBytes,
+                              pitch, kAugBytes));
+        else
+            m.b1 = m.b0;
         KnnTcParams p{};
         p.base_norms = z.b_norms;
         p.query_norms = z.q_norms;
+        p.query_packed = z.q_packed;
+        p.pitch = static_cast<uint32_t>(pitch);
+        p.data_bytes = static_cast<uint32_t>(data_bytes);
         p.n_base = z.n_b;
         p.base_id0 = static_cast<uint32_t>(z.b_id0);
         p.n_queries = static_cast<uint32_t>(q_count);
@@ -366,7 +422,7 @@ knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int me
         p.query_id0 = static_cast<uint32_t>(z.q_id0);
         p.exclude_self = z.exclude_self;
         p.k = static_cast<uint32_t>(k);
-        p.kchunks = static_cast<uint32_t>(pitch / kChunkBytes);
+        p.kchunks = static_cast<uint32_t>(data_bytes / kChunkBytes);
         p.out_ids = ids;
         p.out_dists = dists;
         p.fallback_rows = sc.fallback_rows;
@@ -382,10 +438,11 @@ knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int me
         // (305 ms vs 263 ms: the 96-register budget spills), so off by default.
         int split = 1;
         if (const char* sv = std::getenv("KNNG_GPU_SPLIT")) split = (std::atoi(sv) == 2 && mt == 2 && k <= 16) ? 2 : 1;
-        p.stages = pick_stages(1, mt, false, p.kchunks, split, split > 1 ? (k <= 10 ? 10 : 16) : 0);
+        const bool aug = metric == 0;
+        p.stages = pick_stages(1, mt, false, p.kchunks, split, split > 1 ? (k <= 10 ? 10 : 16) : 0, aug);
         if (split > 1 && p.stages < 3) {
             split = 1;
-            p.stages = pick_stages(1, mt, false, p.kchunks);
+            p.stages = pick_stages(1, mt, false, p.kchunks, 1, 0, aug);
         }
         if (p.stages < 2 || (mt > 1 && p.stages < p.kchunks))
             return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: shared memory budget exceeded");
@@ -573,8 +630,8 @@ knng_gpu_status knn_f32_impl(const float* x, uint64_t n, uint64_t d, uint64_t q_
     }
     // Candidate filter on the tensor cores.
     TcMaps m;
-    KNNG_TRY(make_map(&m.b0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sc.hi, n, pitch));
-    KNNG_TRY(make_map(&m.b1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sc.lo, n, pitch));
+    KNNG_TRY(make_map(&m.b0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sc.hi, n, pitch, pitch * 2));
+    KNNG_TRY(make_map(&m.b1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sc.lo, n, pitch, pitch * 2));
     m.q0 = m.b0;
     m.q1 = m.b1;
     KnnTcParams p{};
@@ -703,10 +760,14 @@ knng_gpu_status pack_impl(const float* x, uint64_t rows, uint64_t d, uint8_t* pa
 {
     if (rows == 0) return KNNG_GPU_OK;
     const uint64_t pitch = knng_gpu_padded_dim(d);
+    const uint64_t data_bytes = u8_data_bytes(d);
     const uint64_t warps_needed = rows;
     const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((warps_needed + 7) / 8, 148ull * 16));
-    pack_u8_kernel<<<blocks, 256, 0, st>>>(x, rows, static_cast<uint32_t>(d), static_cast<uint32_t>(pitch), packed,
-                                          norms, nonint);
+    pack_u8_kernel<<<blocks, 256, 0, st>>>(x, rows, static_cast<uint32_t>(d), static_cast<uint32_t>(data_bytes),
+                                          static_cast<uint32_t>(pitch), packed, norms, nonint);
+    KNNG_CUDA(cudaGetLastError());
+    pack_aug_kernel<<<static_cast<uint32_t>((rows + 127) / 128), 128, 0, st>>>(
+        rows, static_cast<uint32_t>(data_bytes), static_cast<uint32_t>(pitch), packed, norms);
     KNNG_CUDA(cudaGetLastError());
     return KNNG_GPU_OK;
 }
@@ -734,7 +795,7 @@ knng_gpu_status device_pipeline(const float* x, uint64_t n, uint64_t d, uint64_t
     KNNG_CUDA(cudaStreamSynchronize(st));
     if (stats) {
         std::memset(stats, 0, sizeof(*stats));
-        stats->kernel_launches = 1;
+        stats->kernel_launches = 2;  // pack + augmentation
     }
     if (nonint == 0) {
         KNNG_TRY(knn_u8_impl(packed, norms, n, d, 0, n, k, metric, ids, dists, base + w.scratch, w.total - w.scratch,
@@ -824,7 +885,7 @@ int knng_gpu_device_count(void)
     return c;
 }
 
-uint64_t knng_gpu_padded_dim(uint64_t d) { return align_up(d == 0 ? 1 : d, kChunkBytes); }
+uint64_t knng_gpu_padded_dim(uint64_t d) { return u8_data_bytes(d) + kAugBytes; }
 
 uint64_t knng_gpu_workspace_bytes(uint64_t n, uint64_t d, uint64_t k) { return workspace_layout(n, d, k).total; }
 

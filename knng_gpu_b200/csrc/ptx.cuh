@@ -191,6 +191,10 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (UMMA operand reads, TMA).
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -204,6 +208,19 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr)
     desc |= static_cast<uint64_t>(1024u >> 4) << 32;          // stride byte offset: 8 rows x 128 B
     desc |= static_cast<uint64_t>(1u) << 46;                  // descriptor version (sm_100)
     desc |= static_cast<uint64_t>(2u) << 61;                  // layout: 128-byte swizzle
+    return desc;
+}
+
+// Shared-memory matrix descriptor for a K-major operand of 32-byte rows
+// written by TMA with 32-byte swizzle: 8-row groups 256 bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_sw32(uint32_t saddr)
+{
+    uint64_t desc = 0;
+    desc |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);   // start address
+    desc |= static_cast<uint64_t>(1u) << 16;                  // leading byte offset (one K atom: unused)
+    desc |= static_cast<uint64_t>(256u >> 4) << 32;           // stride byte offset: 8 rows x 32 B
+    desc |= static_cast<uint64_t>(1u) << 46;                  // descriptor version (sm_100)
+    desc |= static_cast<uint64_t>(6u) << 61;                  // layout: 32-byte swizzle
     return desc;
 }
 

@@ -33,8 +33,9 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_padded_dim_and_workspace():
-    assert padded_dim(1) == 128 and padded_dim(128) == 128 and padded_dim(129) == 256
-    assert padded_dim(960) == 1024 and padded_dim(784) == 896
+    # data rounded up to 128 bytes, then 32 bytes of augmentation
+    assert padded_dim(1) == 160 and padded_dim(128) == 160 and padded_dim(129) == 288
+    assert padded_dim(960) == 1056 and padded_dim(784) == 928
     assert workspace_bytes(1000, 128, 10) >= 1000 * 128 + 1000 * 4
     assert workspace_bytes(1000, 960, 100) >= 2 * 1000 * 1024 * 2  # fp32 path: bf16 hi + lo planes
 
