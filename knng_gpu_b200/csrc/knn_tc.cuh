@@ -683,16 +683,22 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                     constexpr int W = decltype(w_tag)::value;
                     if constexpr (!Elem::kFloat) {
                         if (tree_max<W>(v) > lim && !(p.debug_flags & 2u)) {
+                            // Only the 32-column groups that hold a candidate.
 #pragma unroll
-                            for (int i4 = 0; i4 < W / 4; ++i4) {
-                                const int4 nn = nb4[c0 / 4 + i4];
-                                v[4 * i4 + 0] = key_of(v[4 * i4 + 0], nn.x);
-                                v[4 * i4 + 1] = key_of(v[4 * i4 + 1], nn.y);
-                                v[4 * i4 + 2] = key_of(v[4 * i4 + 2], nn.z);
-                                v[4 * i4 + 3] = key_of(v[4 * i4 + 3], nn.w);
+                            for (int c = 0; c < W / 32; ++c) {
+                                int32_t* vc = v + c * 32;
+                                if (W > 32 && tree_max<32>(vc) <= lim) continue;
+#pragma unroll
+                                for (int i4 = 0; i4 < 8; ++i4) {
+                                    const int4 nn = nb4[(c0 + c * 32) / 4 + i4];
+                                    vc[4 * i4 + 0] = key_of(vc[4 * i4 + 0], nn.x);
+                                    vc[4 * i4 + 1] = key_of(vc[4 * i4 + 1], nn.y);
+                                    vc[4 * i4 + 2] = key_of(vc[4 * i4 + 2], nn.z);
+                                    vc[4 * i4 + 3] = key_of(vc[4 * i4 + 3], nn.w);
+                                }
+                                insert_keys(vc, std::integral_constant<int, 32>{}, c0 + c * 32);
+                                lim = lim_of(thr);
                             }
-                            insert_keys(v, w_tag, c0);
-                            lim = lim_of(thr);
                         }
                     } else {
 #pragma unroll
