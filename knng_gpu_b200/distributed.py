@@ -41,9 +41,18 @@ def compute_shard(global_n: int, num_ranks: int, rank: int) -> ShardBounds:
     return ShardBounds(rank * base, base + (rem if rank == num_ranks - 1 else 0))
 
 
+SLICE_ALIGN = 256
+
+
 def slice_rows(global_n: int, num_ranks: int) -> int:
-    """Rows per rank in the equal-size slices that are packed and all-gathered."""
-    return (global_n + num_ranks - 1) // num_ranks
+    """Rows per rank in the equal-size slices that are packed and all-gathered:
+    ceil(n / ranks) rounded up to SLICE_ALIGN rows, so every slice starts on a
+    base-tile boundary of the fused kernel (the pack derives each 128-row
+    tile's augmentation offset from that tile alone; tiles that straddle two
+    packs stay exact but filter less sharply). Trailing ranks may get an empty
+    slice when n is small."""
+    per = (global_n + num_ranks - 1) // num_ranks
+    return (per + SLICE_ALIGN - 1) // SLICE_ALIGN * SLICE_ALIGN
 
 
 def gather_shards(local: torch.Tensor, n: int, world: int, group=None) -> torch.Tensor:

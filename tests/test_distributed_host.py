@@ -27,7 +27,7 @@ def test_compute_shard_matches_reference_rule():
             shards = [compute_shard(n, p, r) for r in range(p)]
             assert sum(s.count for s in shards) == n
             assert all(shards[r].start + shards[r].count == shards[r + 1].start for r in range(p - 1))
-    assert slice_rows(10, 4) == 3
+    assert slice_rows(10, 4) == 256 and slice_rows(1000, 2) == 512 and slice_rows(1_000_000, 8) == 125_184
 
 
 def _worker(rank, world, port, n, d, k, q):
