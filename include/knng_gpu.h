@@ -100,10 +100,19 @@ knng_gpu_status knng_gpu_brute_force_device(const float* d_data, uint64_t n, uin
  * shard against the full base, mirroring the reference's query sharding
  * (include/knng/dist/sharded_dataset.hpp:145-155, src/dist/brute_force_mpi.cpp:36-142).
  *
- * knng_gpu_padded_dim: row pitch in bytes of the packed u8 layout (d rounded up to 128).
- * knng_gpu_pack_u8: rows x d fp32 -> rows x pitch u8 + int32 |x|^2 per row;
+ * knng_gpu_padded_dim: row pitch in bytes of the packed u8 layout: the row's
+ *   d bytes rounded up to 128, then 32 bytes of augmentation.
+ * knng_gpu_pack_u8: rows x d fp32 -> rows x pitch u8 + one int32 per row;
  *   atomically ORs 1 into *d_nonint if any value is not an integer in [0,255]
  *   (then the packed output is meaningless and the fp32 path must be used).
+ *   The int32 is the row's key offset keyoff = |x|^2 + 510 * S, where S is
+ *   the sum of the row's augmentation bytes: the packed set computes
+ *   squared L2 as keyoff(r) - 2 (q.r + 255 S(r)) on the tensor cores. S is
+ *   chosen per 128-row tile of the pack call (the tile's largest
+ *   ceil(|x|^2/2) minus the row's, over 255, at most 8160), so packs whose
+ *   first row sits on a multiple of 128 of the searched base filter most
+ *   sharply; any split stays exact. Pass these arrays as the d_norms /
+ *   d_q_norms / d_b_norms arguments below.
  * knng_gpu_knn_u8: queries are packed rows [q_begin, q_begin+q_count) of the
  *   base; results for query row i go to row i of d_ids/d_dists (q_count x k).
  *   d_scratch: >= knng_gpu_knn_scratch_bytes(q_count) bytes.
