@@ -213,6 +213,11 @@ struct ScratchU8 {
     uint32_t* counters;  // [0] fallback count, [1] error flag
 };
 
+// Concurrent base ranges for the last partial wave of query tiles.
+constexpr int kMaxTailParts = 8;
+
+// Fallback-row list (one entry per query) + 2 counters per launch (at most
+// kMaxTailParts + 1 launches: 72 bytes of the 256).
 uint64_t scratch_u8_bytes(uint64_t q_count) { return align_up(q_count * 4, 256) + 256; }
 
 ScratchU8 carve_scratch_u8(void* p, uint64_t q_count)
@@ -310,9 +315,11 @@ knng_gpu_status launch_exact(const KnnExactParams<T>& p, int metric, uint32_t ma
 // the exact kernel on the packed bytes.
 constexpr uint64_t kMaxTensorDim = 1024;
 
+// Device interval timer; ms() is 0 unless both ends were recorded (an
+// elapsed-time query on an unrecorded event would leave a sticky error).
 struct EventTimer {
     cudaEvent_t a = nullptr, b = nullptr;
-    bool on;
+    bool on, started = false, stopped = false;
     explicit EventTimer(bool enable) : on(enable)
     {
         if (on) {
@@ -327,16 +334,16 @@ struct EventTimer {
     }
     void start(cudaStream_t s)
     {
-        if (on) cudaEventRecord(a, s);
+        if (on) started = cudaEventRecord(a, s) == cudaSuccess;
     }
     void stop(cudaStream_t s)
     {
-        if (on) cudaEventRecord(b, s);
+        if (on) stopped = cudaEventRecord(b, s) == cudaSuccess;
     }
     float ms()
     {
         float m = 0.f;
-        if (on) {
+        if (on && started && stopped) {
             cudaEventSynchronize(b);
             cudaEventElapsedTime(&m, a, b);
         }
@@ -368,21 +375,25 @@ struct U8Sets {
     int exclude_self;
 };
 
-knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int metric, uint32_t* ids, float* dists,
-                                 void* scratch, uint64_t scratch_bytes, cudaStream_t st, knng_gpu_stats* stats)
+// Query tiles per CTA of the fused u8 kernel: two need k <= 32 (register
+// budget of 320 threads) and at most two K chunks of resident A.
+int u8_query_tiles_per_cta(uint64_t d, uint64_t k)
+{
+    int mt = (u8_data_bytes(d) / kChunkBytes <= 2 && k <= 32) ? 2 : 1;
+    if (const char* mv = std::getenv("KNNG_GPU_MT")) mt = std::atoi(mv) == 1 ? 1 : mt;  // experiments only
+    return mt;
+}
+
+// Launch the u8 search of one (query set, base set) pair on `st`: the fused
+// tensor-core kernel, then the exact kernel for the rows it flags (device-side
+// count), or the exact kernel alone for d > kMaxTensorDim. No host sync; the
+// caller zeroes sc.counters before and reads them after. tf (optional) times
+// the exact pass.
+knng_gpu_status launch_u8_sets(const U8Sets& z, uint64_t d, uint64_t k, int metric, uint32_t* ids, float* dists,
+                               const ScratchU8& sc, cudaStream_t st, uint32_t* launches, EventTimer* tf)
 {
     const uint64_t q_count = z.n_q;
-    if (scratch_bytes < scratch_u8_bytes(q_count))
-        return fail(KNNG_GPU_WORKSPACE_TOO_SMALL, "knng::gpu: scratch smaller than knng_gpu_knn_scratch_bytes");
-    if (q_count == 0) return KNNG_GPU_OK;
-    if (z.n_b < k + (z.exclude_self ? 1 : 0))
-        return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: fewer base rows than k");
     const uint64_t pitch = knng_gpu_padded_dim(d);
-    ScratchU8 sc = carve_scratch_u8(scratch, q_count);
-    KNNG_CUDA(cudaMemsetAsync(sc.counters, 0, 8, st));
-    uint32_t launches = 1;
-    EventTimer tk(stats != nullptr), tf(stats != nullptr);
-    tk.start(st);
     KnnExactParams<uint8_t> e{};
     e.base = z.b_packed;
     e.base_stride = pitch;
@@ -429,9 +440,7 @@ knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int me
         p.fallback_count = sc.counters;
         p.error = reinterpret_cast<int*>(sc.counters + 1);
         if (const char* dbg = std::getenv("KNNG_GPU_DEBUG_FLAGS")) p.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
-        // Two query tiles per CTA need k <= 32 (register budget of 320 threads).
-        int mt = (p.kchunks <= 2 && k <= 32) ? 2 : 1;
-        if (const char* mv = std::getenv("KNNG_GPU_MT")) mt = std::atoi(mv) == 1 ? 1 : mt;  // experiments only
+        int mt = u8_query_tiles_per_cta(d, k);
         // Optional column-split epilogue (four epilogue warps per SM
         // sub-partition, each on half of a 256-column tile), KNNG_GPU_SPLIT=2.
         // Measured slower than one warp per 32 rows at n=1M d=128 k=10 on B200
@@ -468,21 +477,152 @@ knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int me
                          h[0], h[1], h[2], h[3], h[4], h[5], h[6]);
             cudaFree(dbg_clk);
         }
-        tk.stop(st);
         // Rows whose fp32 sums may round: recompute exactly (device-side
         // count; CTAs past it exit at once).
-        tf.start(st);
+        if (tf) tf->start(st);
         e.row_list = sc.fallback_rows;
         e.row_count = sc.counters;
         KNNG_TRY(launch_exact(e, metric, static_cast<uint32_t>(q_count), st));
-        tf.stop(st);
-        launches = 2;
+        if (tf) tf->stop(st);
+        *launches += 2;
     } else {
         KNNG_TRY(launch_exact(e, metric, static_cast<uint32_t>(q_count), st));
-        tk.stop(st);
-        tf.start(st);
-        tf.stop(st);
+        *launches += 1;
     }
+    return KNNG_GPU_OK;
+}
+
+__global__ void merge_topk_kernel(const uint32_t* __restrict__ a_ids, const float* __restrict__ a_d,
+                                  const uint32_t* __restrict__ b_ids, const float* __restrict__ b_d, uint64_t rows,
+                                  uint32_t k, uint32_t* __restrict__ o_ids, float* __restrict__ o_d);
+
+// Streams and events of one split search, released on every exit path.
+struct ForkSet {
+    cudaStream_t s[kMaxTailParts] = {};
+    cudaEvent_t fork = nullptr, join[kMaxTailParts] = {};
+    ~ForkSet()
+    {
+        for (int i = 0; i < kMaxTailParts; ++i) {
+            if (join[i]) cudaEventDestroy(join[i]);
+            if (s[i]) cudaStreamDestroy(s[i]);
+        }
+        if (fork) cudaEventDestroy(fork);
+    }
+};
+
+// u8 search of a query set against a base set. The fused kernel is
+// persistent with one CTA per SM over query tiles; when the last wave would
+// hold only R < SMs/2 tiles, those tail queries are searched first by
+// f = SMs / R concurrent launches, each over one 256-row-aligned range of the
+// base, and the f exact partial lists are merged by (distance, id). Their
+// temporary rows live in the output rows of the main range, which the main
+// launch then overwrites. The result is identical to one pass.
+knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int metric, uint32_t* ids, float* dists,
+                                 void* scratch, uint64_t scratch_bytes, cudaStream_t st, knng_gpu_stats* stats,
+                                 bool allow_split = true)
+{
+    const uint64_t q_count = z.n_q;
+    if (scratch_bytes < scratch_u8_bytes(q_count))
+        return fail(KNNG_GPU_WORKSPACE_TOO_SMALL, "knng::gpu: scratch smaller than knng_gpu_knn_scratch_bytes");
+    if (q_count == 0) return KNNG_GPU_OK;
+    if (z.n_b < k + (z.exclude_self ? 1 : 0))
+        return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: fewer base rows than k");
+    const uint64_t pitch = knng_gpu_padded_dim(d);
+    const ScratchU8 sc = carve_scratch_u8(scratch, q_count);
+    // Tail plan.
+    const uint64_t sms = static_cast<uint64_t>(sm_count());
+    const uint64_t qt_rows = static_cast<uint64_t>(u8_query_tiles_per_cta(d, k)) * kTileRows;
+    const uint64_t qtiles = (q_count + qt_rows - 1) / qt_rows;
+    const uint64_t full_waves = qtiles / sms, tail_tiles = qtiles % sms;
+    uint64_t parts = tail_tiles ? std::min<uint64_t>(kMaxTailParts, sms / tail_tiles) : 0;
+    uint64_t part_rows = 0;
+    if (parts >= 2) {
+        part_rows = align_up((z.n_b + parts - 1) / parts, 256);
+        parts = (z.n_b + part_rows - 1) / part_rows;
+        // every part needs k (+ self) rows
+        if (part_rows < k + 1 || z.n_b - (parts - 1) * part_rows < k + 1) parts = 0;
+    }
+    bool split = allow_split && d <= kMaxTensorDim && full_waves >= 1 && parts >= 2;
+    if (const char* tv = std::getenv("KNNG_GPU_TAIL_SPLIT")) split = split && std::atoi(tv) != 0;  // experiments
+    const uint64_t main_q = split ? full_waves * sms * qt_rows : q_count;
+    const uint64_t tail_q = q_count - main_q;
+    const uint32_t n_launch = split ? static_cast<uint32_t>(parts) + 1 : 1;
+    KNNG_CUDA(cudaMemsetAsync(sc.counters, 0, 8 * n_launch, st));
+    uint32_t launches = 0;
+    EventTimer tk(stats != nullptr), tf(stats != nullptr && !split);
+    tk.start(st);
+    if (split) {
+        ForkSet fs;
+        KNNG_CUDA(cudaEventCreateWithFlags(&fs.fork, cudaEventDisableTiming));
+        KNNG_CUDA(cudaEventRecord(fs.fork, st));
+        for (uint64_t pi = 0; pi < parts; ++pi) {
+            KNNG_CUDA(cudaStreamCreateWithFlags(&fs.s[pi], cudaStreamNonBlocking));
+            KNNG_CUDA(cudaEventCreateWithFlags(&fs.join[pi], cudaEventDisableTiming));
+            KNNG_CUDA(cudaStreamWaitEvent(fs.s[pi], fs.fork, 0));
+            const uint64_t b0 = pi * part_rows;
+            U8Sets zp = z;
+            zp.q_packed = z.q_packed + main_q * pitch;
+            zp.q_norms = z.q_norms + main_q;
+            zp.n_q = tail_q;
+            zp.q_id0 = z.q_id0 + main_q;
+            zp.b_packed = z.b_packed + b0 * pitch;
+            zp.b_norms = z.b_norms + b0;
+            zp.n_b = std::min(part_rows, z.n_b - b0);
+            zp.b_id0 = z.b_id0 + b0;
+            const ScratchU8 scp{sc.fallback_rows + pi * tail_q, sc.counters + 2 * (1 + pi)};
+            KNNG_TRY(launch_u8_sets(zp, d, k, metric, ids + pi * tail_q * k, dists + pi * tail_q * k, scp, fs.s[pi],
+                                    &launches, nullptr));
+            KNNG_CUDA(cudaEventRecord(fs.join[pi], fs.s[pi]));
+            KNNG_CUDA(cudaStreamWaitEvent(st, fs.join[pi], 0));
+        }
+        // Fold the partial lists into the tail rows, alternating between the
+        // tail rows and part 0's temporary rows (free after the first merge)
+        // so that no merge writes the list it reads.
+        uint32_t* t_ids = ids + main_q * k;
+        float* t_d = dists + main_q * k;
+        const uint32_t blocks = static_cast<uint32_t>((tail_q + 255) / 256);
+        bool in_tail = false;  // the running result: part 0's rows at first
+        for (uint64_t pi = 1; pi < parts; ++pi) {
+            const uint32_t* a_ids = in_tail ? t_ids : ids;
+            const float* a_d = in_tail ? t_d : dists;
+            uint32_t* o_ids = in_tail ? ids : t_ids;
+            float* o_d = in_tail ? dists : t_d;
+            merge_topk_kernel<<<blocks, 256, 0, st>>>(a_ids, a_d, ids + pi * tail_q * k, dists + pi * tail_q * k,
+                                                      tail_q, static_cast<uint32_t>(k), o_ids, o_d);
+            KNNG_CUDA(cudaGetLastError());
+            ++launches;
+            in_tail = !in_tail;
+        }
+        if (!in_tail) {
+            KNNG_CUDA(cudaMemcpyAsync(t_ids, ids, tail_q * k * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+            KNNG_CUDA(cudaMemcpyAsync(t_d, dists, tail_q * k * sizeof(float), cudaMemcpyDeviceToDevice, st));
+        }
+        U8Sets zm = z;
+        zm.n_q = main_q;
+        KNNG_TRY(launch_u8_sets(zm, d, k, metric, ids, dists, ScratchU8{sc.fallback_rows, sc.counters}, st,
+                                &launches, nullptr));
+        tk.stop(st);
+        uint32_t host_counters[2 * (kMaxTailParts + 1)] = {};
+        KNNG_CUDA(cudaMemcpyAsync(host_counters, sc.counters, 8 * n_launch, cudaMemcpyDeviceToHost, st));
+        KNNG_CUDA(cudaStreamSynchronize(st));
+        uint32_t fallback = 0;
+        for (uint32_t i = 0; i < n_launch; ++i) {
+            if (host_counters[2 * i + 1] != 0)
+                return fail(KNNG_GPU_TIMEOUT, "knng::gpu: a bounded device wait gave up (code " +
+                                                  std::to_string(host_counters[2 * i + 1]) + ")");
+            fallback += host_counters[2 * i];
+        }
+        if (stats) {
+            stats->path = KNNG_PATH_U8_TENSOR;
+            stats->fallback_rows = fallback;
+            stats->knn_ms = tk.ms();
+            stats->fallback_ms = 0.f;
+            stats->kernel_launches += launches;
+        }
+        return KNNG_GPU_OK;
+    }
+    KNNG_TRY(launch_u8_sets(z, d, k, metric, ids, dists, sc, st, &launches, &tf));
+    tk.stop(st);
     uint32_t host_counters[2] = {0, 0};
     KNNG_TRY(read_counters(sc.counters, host_counters, st));
     if (stats) {
@@ -497,12 +637,12 @@ knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int me
 
 knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_t n, uint64_t d, uint64_t q_begin,
                             uint64_t q_count, uint64_t k, int metric, uint32_t* ids, float* dists, void* scratch,
-                            uint64_t scratch_bytes, cudaStream_t st, knng_gpu_stats* stats)
+                            uint64_t scratch_bytes, cudaStream_t st, knng_gpu_stats* stats, bool allow_split = true)
 {
     if (q_begin + q_count > n) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: query range exceeds the base");
     const uint64_t pitch = knng_gpu_padded_dim(d);
     const U8Sets z{packed + q_begin * pitch, norms + q_begin, q_count, q_begin, packed, norms, n, 0, 1};
-    return knn_u8_sets_impl(z, d, k, metric, ids, dists, scratch, scratch_bytes, st, stats);
+    return knn_u8_sets_impl(z, d, k, metric, ids, dists, scratch, scratch_bytes, st, stats, allow_split);
 }
 
 // Merge two row-wise sorted k-lists into the k best by (distance, id) -- the
@@ -1004,8 +1144,9 @@ knng_gpu_status knng_gpu_knn_u8_noalloc(const uint8_t* d_packed, const int32_t* 
     KNNG_TRY(noalloc_scratch_ptr(&scratch));
     // knn_u8_impl zeroes the counters on `stream` before the kernel runs, so
     // the previous call's contents never leak into this one.
+    // No tail split here: it would create streams and events.
     return knn_u8_impl(d_packed, d_norms, n, d, q_begin, q_count, k, metric, d_ids, d_dists, scratch,
-                       kNoAllocScratchBytes, static_cast<cudaStream_t>(stream), stats);
+                       kNoAllocScratchBytes, static_cast<cudaStream_t>(stream), stats, false);
 }
 
 knng_gpu_status knng_gpu_knn_u8_sets(const uint8_t* d_q_packed, const int32_t* d_q_norms, uint64_t n_q,

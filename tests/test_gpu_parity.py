@@ -140,3 +140,22 @@ def test_config3_subset_against_oracle(cuda_ok):
     oi, od = oracle_knn(x, cfg.k, cfg.metric, queries=q)
     assert np.array_equal(ids[q.astype(np.int64)], oi)
     assert np.array_equal(dists[q.astype(np.int64)], od)
+
+
+@pytest.mark.parametrize("metric", [0, 1])
+def test_tail_split_against_oracle_and_single_pass(cuda_ok, metric, monkeypatch):
+    """n = 40,000 rows give one full wave of 256-row query tiles on 148 SMs
+    plus a 9-tile tail, which is searched as 8 concurrent base ranges and
+    merged. Every row must equal the unsplit search, and rows from both the
+    main range and the tail must equal the oracle."""
+    n, d, k = 40_000, 128, 10
+    kind = syn.KIND_UNIFORM_INT if metric == 0 else syn.KIND_SPARSE_INT
+    x = syn.generate(kind, 77, n, d, p_zero=0.6)
+    ids, dists, _ = run_gpu(x, k, metric)
+    monkeypatch.setenv("KNNG_GPU_TAIL_SPLIT", "0")
+    ids1, dists1, _ = run_gpu(x, k, metric)
+    assert np.array_equal(ids, ids1) and np.array_equal(dists, dists1)
+    q = np.concatenate([syn.sample_ids(5, 37_888, 32), 37_888 + syn.sample_ids(6, n - 37_888, 32)])
+    oi, od = oracle_knn(x, k, metric, queries=q)
+    assert np.array_equal(ids[q.astype(np.int64)], oi)
+    assert np.array_equal(dists[q.astype(np.int64)], od)
