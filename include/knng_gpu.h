@@ -78,6 +78,15 @@ int knng_gpu_device_count(void);
 knng_gpu_status knng_gpu_brute_force(const float* data, uint64_t n, uint64_t d, uint64_t k, int metric,
                                      uint32_t* ids, float* dists, knng_gpu_stats* stats);
 
+/* Same build from rows that are already bytes (.bvecs records: the u8 path
+ * without the fp32 round trip, src/io/fvecs.cpp:189-206 reads them into
+ * floats). Row r's d values start at rows + r * row_stride (row_stride >= d;
+ * d + 4 passes a .bvecs payload with its per-row dimension headers after
+ * skipping the first header). Output identical to knng_gpu_brute_force on the
+ * same values as floats. */
+knng_gpu_status knng_gpu_brute_force_u8(const uint8_t* rows, uint64_t n, uint64_t d, uint64_t row_stride, uint64_t k,
+                                        int metric, uint32_t* ids, float* dists, knng_gpu_stats* stats);
+
 /* Free the device buffers and stream that knng_gpu_brute_force keeps per
  * device between calls (they are grown on demand and otherwise held until
  * process exit). No counterpart in the reference. */
@@ -124,6 +133,10 @@ knng_gpu_status knng_gpu_brute_force_device(const float* d_data, uint64_t n, uin
 uint64_t knng_gpu_padded_dim(uint64_t d);
 knng_gpu_status knng_gpu_pack_u8(const float* d_x, uint64_t rows, uint64_t d, uint8_t* d_packed,
                                  int32_t* d_norms, int32_t* d_nonint, void* stream);
+/* knng_gpu_pack_u8_bytes: as knng_gpu_pack_u8 for device rows that are
+ *   already bytes (row r at d_rows + r * row_stride, row_stride >= d). */
+knng_gpu_status knng_gpu_pack_u8_bytes(const uint8_t* d_rows, uint64_t rows, uint64_t d, uint64_t row_stride,
+                                       uint8_t* d_packed, int32_t* d_norms, void* stream);
 uint64_t knng_gpu_knn_scratch_bytes(uint64_t q_count);
 knng_gpu_status knng_gpu_knn_u8(const uint8_t* d_packed, const int32_t* d_norms, uint64_t n, uint64_t d,
                                 uint64_t q_begin, uint64_t q_count, uint64_t k, int metric, uint32_t* d_ids,

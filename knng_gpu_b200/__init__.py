@@ -13,6 +13,7 @@ from .api import (  # noqa: F401
     NegativeInnerProduct,
     brute_force_knn,
     brute_force_knn_device,
+    brute_force_knn_u8,
     device_count,
     knn_f32,
     knn_f32_scratch_bytes,
@@ -21,6 +22,7 @@ from .api import (  # noqa: F401
     knn_u8_sets,
     merge_topk,
     pack_u8,
+    pack_u8_bytes,
     padded_dim,
     workspace_bytes,
 )

@@ -32,6 +32,8 @@ GPU_SYMBOLS = (
     "knng_gpu_knn_f32_scratch_bytes",
     "knng_gpu_knn_f32",
     "knng_gpu_knn_u8_noalloc",
+    "knng_gpu_brute_force_u8",
+    "knng_gpu_pack_u8_bytes",
 )
 
 
@@ -84,6 +86,9 @@ def gpu_lib() -> ctypes.CDLL:
             "knng_gpu_padded_dim": (c_uint64, [c_uint64]),
             "knng_gpu_pack_u8": (c_int, [c_void_p, c_uint64, c_uint64, c_void_p, c_void_p, c_void_p, c_void_p]),
             "knng_gpu_knn_scratch_bytes": (c_uint64, [c_uint64]),
+            "knng_gpu_brute_force_u8": (
+                c_int, [c_void_p, c_uint64, c_uint64, c_uint64, c_uint64, c_int, c_void_p, c_void_p, st]),
+            "knng_gpu_pack_u8_bytes": (c_int, [c_void_p, c_uint64, c_uint64, c_uint64, c_void_p, c_void_p, c_void_p]),
             "knng_gpu_knn_u8": (
                 c_int,
                 [c_void_p, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64, c_uint64, c_int, c_void_p, c_void_p,

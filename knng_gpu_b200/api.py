@@ -147,6 +147,28 @@ def brute_force_knn(ds: Dataset | np.ndarray, k: int, distance=L2Squared()) -> K
     return Knng(n, k, ids[: n * k], dists[: n * k], stats.as_dict())
 
 
+def brute_force_knn_u8(rows: np.ndarray, k: int, distance=L2Squared(), d: int | None = None) -> Knng:
+    """As :func:`brute_force_knn` for rows that are already bytes (u8 path
+    without the fp32 round trip). ``rows``: a contiguous uint8 array of shape
+    (n, d), or of shape (n, stride) with the values in the first ``d`` bytes
+    of each row (e.g. a .bvecs payload viewed as (n, d + 4) after its first
+    4-byte header). Same output as :func:`brute_force_knn` on the same values."""
+    rows = np.ascontiguousarray(rows, dtype=np.uint8)
+    if rows.ndim != 2:
+        raise InvalidArgument("brute_force_knn_u8: rows must be 2-D")
+    n, stride = int(rows.shape[0]), int(rows.shape[1])
+    d = stride if d is None else int(d)
+    if k < 0:
+        raise InvalidArgument("knng::gpu::brute_force_knn: k must be > 0")
+    ids = np.empty(max(n * k, 1), dtype=np.uint32)
+    dists = np.empty(max(n * k, 1), dtype=np.float32)
+    stats = KnngGpuStats()
+    check(gpu_lib().knng_gpu_brute_force_u8(rows.ctypes.data if rows.size else None, n, d, stride, k,
+                                            _metric_id(distance), ids.ctypes.data, dists.ctypes.data,
+                                            ctypes.byref(stats)))
+    return Knng(n, k, ids[: n * k], dists[: n * k], stats.as_dict())
+
+
 # ---------------------------------------------------------------- device API
 def _ptr(t) -> int | None:
     return None if t is None else int(t.data_ptr())
@@ -202,6 +224,15 @@ def pack_u8(x, packed, norms, nonint_flag, stream=None) -> None:
     rows, d = x.shape
     check(gpu_lib().knng_gpu_pack_u8(_ptr(x), rows, d, _ptr(packed), _ptr(norms), _ptr(nonint_flag),
                                      _stream_handle(stream)))
+
+
+def pack_u8_bytes(rows, packed, norms, d: int | None = None, stream=None) -> None:
+    """u8 pack + key offsets of a CUDA uint8 (rows, stride) tensor whose first
+    ``d`` bytes per row are the values (no fp32 round trip)."""
+    n, stride = rows.shape
+    d = stride if d is None else d
+    check(gpu_lib().knng_gpu_pack_u8_bytes(_ptr(rows), n, d, stride, _ptr(packed), _ptr(norms),
+                                           _stream_handle(stream)))
 
 
 def knn_scratch_bytes(q_count: int) -> int:

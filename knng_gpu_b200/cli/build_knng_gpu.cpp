@@ -125,16 +125,16 @@ int main(int argc, char** argv)
     }
     try {
         std::cerr << "build_knng_gpu: loading " << args.dataset << '\n';
+        // .bvecs rows stay bytes all the way to the device (u8 ingest, no
+        // float round trip); .fvecs rows go through the fp32 entry point.
         std::vector<float> x;
+        std::vector<std::uint8_t> raw;
+        const bool bytes = ends_with(args.dataset, ".bvecs");
         std::uint64_t n = 0, d = 0;
-        if (ends_with(args.dataset, ".bvecs")) {
-            std::vector<std::uint8_t> raw;
+        if (bytes)
             knng_files::read_vecs<std::uint8_t>(args.dataset, raw, n, d);
-            x.resize(raw.size());
-            for (std::size_t i = 0; i < raw.size(); ++i) x[i] = static_cast<float>(raw[i]);
-        } else {
+        else
             knng_files::read_vecs<float>(args.dataset, x, n, d);
-        }
         std::cerr << "build_knng_gpu: loaded n=" << n << " d=" << d << '\n';
         if (cudaSetDevice(args.device) != cudaSuccess) throw std::runtime_error("cudaSetDevice failed");
         const std::uint32_t metric = args.metric == "l2" ? KNNG_METRIC_L2_SQUARED : KNNG_METRIC_NEGATIVE_INNER_PRODUCT;
@@ -147,14 +147,19 @@ int main(int argc, char** argv)
         g.dists.resize(n * args.k);
         knng_gpu_stats stats{};
         const knng_gpu_status st =
-            knng_gpu_brute_force(x.data(), n, d, args.k, static_cast<int>(metric), g.ids.data(), g.dists.data(), &stats);
+            bytes ? knng_gpu_brute_force_u8(raw.data(), n, d, d, args.k, static_cast<int>(metric), g.ids.data(),
+                                            g.dists.data(), &stats)
+                  : knng_gpu_brute_force(x.data(), n, d, args.k, static_cast<int>(metric), g.ids.data(),
+                                         g.dists.data(), &stats);
         if (st != KNNG_GPU_OK) throw std::runtime_error(knng_gpu_last_error());
         std::cerr << "build_knng_gpu: device time " << stats.total_ms << " ms (path "
                   << (stats.path == KNNG_PATH_U8_TENSOR ? "u8 tensor" : "fp32 tensor") << ")\n";
         std::cerr << "build_knng_gpu: writing " << args.output << '\n';
         knng_files::write_knng(args.output, g, metric, args.algorithm == "brute_force" ? 0u : 1u);
         if (!args.ground_truth.empty()) {
-            knng_files::save_ground_truth(args.ground_truth, g, knng_files::dataset_hash(x.data(), n, d), metric);
+            const std::uint64_t hash =
+                bytes ? knng_files::dataset_hash_u8(raw.data(), n, d) : knng_files::dataset_hash(x.data(), n, d);
+            knng_files::save_ground_truth(args.ground_truth, g, hash, metric);
             std::cerr << "build_knng_gpu: wrote ground truth " << args.ground_truth << '\n';
         }
         std::cerr << "build_knng_gpu: done\n";

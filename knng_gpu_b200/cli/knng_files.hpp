@@ -80,6 +80,20 @@ inline std::uint64_t dataset_hash(const float* x, std::uint64_t n, std::uint64_t
     return s;
 }
 
+// The same hash for u8 rows, over the bytes of their float values (what the
+// reference hashes after loading .bvecs as floats), without a float copy.
+inline std::uint64_t dataset_hash_u8(const std::uint8_t* x, std::uint64_t n, std::uint64_t d)
+{
+    std::uint64_t s = 14695981039346656037ull;
+    s = fnv1a64(s, &n, 8);
+    s = fnv1a64(s, &d, 8);
+    for (std::uint64_t i = 0; i < n * d; ++i) {
+        const float f = static_cast<float>(x[i]);
+        s = fnv1a64(s, &f, 4);
+    }
+    return s;
+}
+
 struct Graph {
     std::uint64_t n = 0, k = 0;
     std::vector<std::uint32_t> ids;

@@ -115,6 +115,37 @@ __global__ void __launch_bounds__(256) pack_u8_kernel(const float* __restrict__ 
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(nonint, 1);
 }
 
+// u8 ingest: rows that are already bytes (a .bvecs file's records, any row
+// stride and byte offset) -> the packed layout + exact int32 |x|^2, with no
+// float round trip. One warp per row; lane l handles bytes 4l..4l+3 of every
+// 128-byte chunk.
+__global__ void __launch_bounds__(256) pack_u8_bytes_kernel(const uint8_t* __restrict__ src, uint64_t rows,
+                                                            uint32_t d, uint64_t row_stride, uint32_t data_bytes,
+                                                            uint32_t pitch, uint8_t* __restrict__ packed,
+                                                            int32_t* __restrict__ norms)
+{
+    const uint32_t lane = threadIdx.x & 31;
+    const uint64_t warp0 = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = (static_cast<uint64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (uint64_t r = warp0; r < rows; r += nwarps) {
+        const uint8_t* xr = src + r * row_stride;
+        int32_t sum = 0;
+        for (uint32_t c0 = lane * 4; c0 < data_bytes; c0 += 128) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t u = c0 + e < d ? static_cast<uint32_t>(xr[c0 + e]) : 0u;
+                sum += static_cast<int32_t>(u * u);
+                word |= u << (8 * e);
+            }
+            *reinterpret_cast<uint32_t*>(packed + r * pitch + c0) = word;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) norms[r] = sum;
+    }
+}
+
 // Augmentation of the packed rows for the tensor-core L2 filter. For each
 // 128-row tile of this pack call, C = max over its rows of ceil(|r|^2 / 2)
 // and S(r) = min(8160, (C - ceil(|r|^2 / 2)) / 255); the row's 32
@@ -912,6 +943,56 @@ knng_gpu_status pack_impl(const float* x, uint64_t rows, uint64_t d, uint8_t* pa
     return KNNG_GPU_OK;
 }
 
+knng_gpu_status pack_bytes_impl(const uint8_t* rows_u8, uint64_t rows, uint64_t d, uint64_t row_stride,
+                                uint8_t* packed, int32_t* norms, cudaStream_t st)
+{
+    if (rows == 0) return KNNG_GPU_OK;
+    const uint64_t pitch = knng_gpu_padded_dim(d);
+    const uint64_t data_bytes = u8_data_bytes(d);
+    const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((rows + 7) / 8, 148ull * 16));
+    pack_u8_bytes_kernel<<<blocks, 256, 0, st>>>(rows_u8, rows, static_cast<uint32_t>(d), row_stride,
+                                                static_cast<uint32_t>(data_bytes), static_cast<uint32_t>(pitch),
+                                                packed, norms);
+    KNNG_CUDA(cudaGetLastError());
+    pack_aug_kernel<<<static_cast<uint32_t>((rows + 127) / 128), 128, 0, st>>>(
+        rows, static_cast<uint32_t>(data_bytes), static_cast<uint32_t>(pitch), packed, norms);
+    KNNG_CUDA(cudaGetLastError());
+    return KNNG_GPU_OK;
+}
+
+// Build from u8 rows already on the device (row_stride bytes apart).
+knng_gpu_status device_pipeline_u8(const uint8_t* rows_u8, uint64_t n, uint64_t d, uint64_t row_stride, uint64_t k,
+                                   int metric, uint32_t* ids, float* dists, void* ws, uint64_t ws_bytes,
+                                   cudaStream_t st, knng_gpu_stats* stats)
+{
+    KNNG_TRY(validate(n, d, k, metric));
+    if (row_stride < d) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: row_stride must be >= d");
+    const WorkspaceLayout w = workspace_layout(n, d, k);
+    if (ws_bytes < w.total || (reinterpret_cast<uintptr_t>(ws) & 255))
+        return fail(KNNG_GPU_WORKSPACE_TOO_SMALL, "knng::gpu: workspace smaller than knng_gpu_workspace_bytes or "
+                                                  "not 256-byte aligned");
+    uint8_t* base = static_cast<uint8_t*>(ws);
+    uint8_t* packed = base + w.packed;
+    int32_t* norms = reinterpret_cast<int32_t*>(base + w.norms);
+    EventTimer tall(stats != nullptr), tp(stats != nullptr);
+    tall.start(st);
+    tp.start(st);
+    KNNG_TRY(pack_bytes_impl(rows_u8, n, d, row_stride, packed, norms, st));
+    tp.stop(st);
+    if (stats) {
+        std::memset(stats, 0, sizeof(*stats));
+        stats->kernel_launches = 2;  // pack + augmentation
+    }
+    KNNG_TRY(knn_u8_impl(packed, norms, n, d, 0, n, k, metric, ids, dists, base + w.scratch, w.total - w.scratch, st,
+                         stats));
+    tall.stop(st);
+    if (stats) {
+        stats->pack_ms = tp.ms();
+        stats->total_ms = tall.ms();
+    }
+    return KNNG_GPU_OK;
+}
+
 knng_gpu_status device_pipeline(const float* x, uint64_t n, uint64_t d, uint64_t k, int metric, uint32_t* ids,
                                 float* dists, void* ws, uint64_t ws_bytes, cudaStream_t st, knng_gpu_stats* stats)
 {
@@ -1102,6 +1183,52 @@ knng_gpu_status knng_gpu_brute_force(const float* data, uint64_t n, uint64_t d, 
     float* ddist = static_cast<float*>(c.dists);
     KNNG_CUDA(cudaMemcpyAsync(dx, data, n * d * sizeof(float), cudaMemcpyHostToDevice, st));
     KNNG_TRY(device_pipeline(dx, n, d, k, metric, dids, ddist, c.ws, c.ws_cap, st, stats));
+    KNNG_CUDA(cudaMemcpyAsync(ids, dids, n * k * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    KNNG_CUDA(cudaMemcpyAsync(dists, ddist, n * k * sizeof(float), cudaMemcpyDeviceToHost, st));
+    KNNG_CUDA(cudaStreamSynchronize(st));
+    return KNNG_GPU_OK;
+}
+
+knng_gpu_status knng_gpu_pack_u8_bytes(const uint8_t* d_rows, uint64_t rows, uint64_t d, uint64_t row_stride,
+                                       uint8_t* d_packed, int32_t* d_norms, void* stream)
+{
+    g_last_error.clear();
+    if (d == 0) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: d must be > 0");
+    if (row_stride < d) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: row_stride must be >= d");
+    return pack_bytes_impl(d_rows, rows, d, row_stride, d_packed, d_norms, static_cast<cudaStream_t>(stream));
+}
+
+knng_gpu_status knng_gpu_brute_force_u8(const uint8_t* rows, uint64_t n, uint64_t d, uint64_t row_stride, uint64_t k,
+                                        int metric, uint32_t* ids, float* dists, knng_gpu_stats* stats)
+{
+    g_last_error.clear();
+    KNNG_TRY(validate(n, d, k, metric));
+    if (row_stride < d) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: row_stride must be >= d");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return fail(KNNG_GPU_CUDA_ERROR, "knng::gpu::brute_force_knn: no CUDA device available");
+    }
+    int dev = 0;
+    KNNG_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: device index out of range");
+    HostCache& c = g_host_cache[dev];
+    std::lock_guard<std::mutex> lock(c.mutex);
+    c.device = dev;
+    if (!c.stream) KNNG_CUDA(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+    cudaStream_t st = c.stream;
+    // The last row needs only d bytes: a .bvecs buffer minus its final header.
+    const uint64_t in_bytes = (n - 1) * row_stride + d;
+    const uint64_t ws_bytes = knng_gpu_workspace_bytes(n, d, k);
+    KNNG_TRY(grow(&c.x, &c.x_cap, in_bytes));
+    KNNG_TRY(grow(&c.ids, &c.ids_cap, n * k * sizeof(uint32_t)));
+    KNNG_TRY(grow(&c.dists, &c.dists_cap, n * k * sizeof(float)));
+    KNNG_TRY(grow(&c.ws, &c.ws_cap, ws_bytes));
+    uint8_t* dx = static_cast<uint8_t*>(c.x);
+    uint32_t* dids = static_cast<uint32_t*>(c.ids);
+    float* ddist = static_cast<float*>(c.dists);
+    KNNG_CUDA(cudaMemcpyAsync(dx, rows, in_bytes, cudaMemcpyHostToDevice, st));
+    KNNG_TRY(device_pipeline_u8(dx, n, d, row_stride, k, metric, dids, ddist, c.ws, c.ws_cap, st, stats));
     KNNG_CUDA(cudaMemcpyAsync(ids, dids, n * k * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
     KNNG_CUDA(cudaMemcpyAsync(dists, ddist, n * k * sizeof(float), cudaMemcpyDeviceToHost, st));
     KNNG_CUDA(cudaStreamSynchronize(st));

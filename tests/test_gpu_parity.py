@@ -159,3 +159,49 @@ def test_tail_split_against_oracle_and_single_pass(cuda_ok, metric, monkeypatch)
     oi, od = oracle_knn(x, k, metric, queries=q)
     assert np.array_equal(ids[q.astype(np.int64)], oi)
     assert np.array_equal(dists[q.astype(np.int64)], od)
+
+
+@pytest.mark.parametrize("metric", [0, 1])
+def test_u8_ingest_matches_float_path(cuda_ok, metric):
+    """Rows given as bytes with a row stride (a .bvecs-like payload: values
+    first, 4 garbage bytes after each row) build the same graph, bit for bit,
+    as the fp32 entry point on the same values, and match the oracle."""
+    n, d, k = 3000, 100, 12
+    rng = np.random.default_rng(11 + metric)
+    vals = rng.integers(0, 256, size=(n, d), dtype=np.uint8)
+    if metric == 1:
+        vals[rng.random((n, d)) < 0.6] = 0
+    buf = np.empty((n, d + 4), dtype=np.uint8)
+    buf[:, :d] = vals
+    buf[:, d:] = rng.integers(0, 256, size=(n, 4), dtype=np.uint8)
+    g = kg.brute_force_knn_u8(buf, k, metric, d=d)
+    assert g.stats["path"] == 0
+    ids, dists, _ = run_gpu(vals.astype(np.float32), k, metric)
+    assert np.array_equal(g.neighbors.reshape(-1, k), ids)
+    assert np.array_equal(g.distances.reshape(-1, k).view(np.uint32), dists.view(np.uint32))
+    q = syn.sample_ids(3, n, 48)
+    oi, od = oracle_knn(vals.astype(np.float32), k, metric, queries=q)
+    assert np.array_equal(ids[q.astype(np.int64)], oi)
+    assert np.array_equal(dists[q.astype(np.int64)], od)
+
+
+def test_u8_ingest_device_pack_matches_float_pack(cuda_ok):
+    """knng_gpu_pack_u8_bytes writes the same packed rows and key offsets as
+    knng_gpu_pack_u8 on the same values."""
+    import torch
+
+    n, d = 1000, 70
+    rng = np.random.default_rng(5)
+    vals = rng.integers(0, 256, size=(n, d), dtype=np.uint8)
+    dev = torch.device("cuda", 0)
+    pitch = kg.padded_dim(d)
+    p1 = torch.zeros((n, pitch), dtype=torch.uint8, device=dev)
+    n1 = torch.zeros(n, dtype=torch.int32, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    kg.pack_u8(torch.from_numpy(vals.astype(np.float32)).to(dev), p1, n1, flag)
+    p2 = torch.zeros((n, pitch), dtype=torch.uint8, device=dev)
+    n2 = torch.zeros(n, dtype=torch.int32, device=dev)
+    kg.pack_u8_bytes(torch.from_numpy(vals).to(dev), p2, n2)
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 0
+    assert torch.equal(p1, p2) and torch.equal(n1, n2)
