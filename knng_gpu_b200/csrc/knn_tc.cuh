@@ -47,6 +47,8 @@ constexpr int kNormRing = 4;        // base-tile norm slots per epilogue warp (p
 constexpr bool kPipelineTmemLoads = false;
 // Small lists: load a whole tile before handing the TMEM buffer back.
 constexpr bool kLoadWholeTile = false;
+// u8, two buffers x two M tiles: a handoff barrier pair per (buffer, M tile).
+constexpr bool kSplitHandoffOpt = true;
 
 struct ElemU8 {
     static constexpr int kPlanes = 1;
@@ -178,6 +180,10 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
     // two TMEM buffers all M tiles of a base tile share one handoff barrier;
     // with one buffer each M tile gets its own so the two tiles alternate.
     constexpr bool kPerMtBars = NBUF == 1 && MT > 1;
+    // Two TMEM buffers and two M tiles (u8): one handoff barrier pair per
+    // (buffer, M tile), so each M tile's epilogue starts when its own MMAs
+    // finish and releases independently of the other M tile.
+    constexpr bool kSplitHandoff = kSplitHandoffOpt && !Elem::kFloat && NBUF == 2 && MT == 2 && SPLIT == 1 && !A_STREAM;
     // SPLIT == 2: two epilogue warps per TMEM lane quarter (four per SM
     // sub-partition instead of two), each filtering half of every tile's
     // columns into its own list; the halves merge at the end of a query tile.
@@ -233,7 +239,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
         mbar_init(a_empty, 1);
         for (int b = 0; b < NBUF * MT; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], kPerMtBars ? 4 : 4 * MT * SPLIT);
+            mbar_init(&tempty[b], (kPerMtBars || kSplitHandoff) ? 4 : 4 * MT * SPLIT);
         }
         *abort_flag = 0;
         *tiles_done = 0;
@@ -407,28 +413,38 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                     // one fence, the MMAs as straight-line code, one commit.
                     for (uint32_t j = 0; j < n_btiles; ++j, ++acc_i) {
                         const uint32_t buf = acc_i & 1u;
-                        if (!mbar_wait_sleep(&tempty[buf], ((acc_i >> 1) & 1u) ^ 1u, abort_flag) ||
-                            !mbar_wait_sleep(&full[s], ph, abort_flag)) {
+                        const uint32_t tpar = ((acc_i >> 1) & 1u) ^ 1u;
+                        if (!mbar_wait_sleep(&full[s], ph, abort_flag) ||
+                            (!kSplitHandoff && !mbar_wait_sleep(&tempty[buf], tpar, abort_flag))) {
                             ok = false;
                             break;
                         }
-                        tc_fence_after();
+                        if (!kSplitHandoff) tc_fence_after();
                         const uint64_t bd = b_desc0 + s * stage_step;
                         const uint32_t d0 = tmem_base + buf * (MT * BN);
                         const uint64_t bd_aug = b_aug_desc0 + s * stage_step;
 #pragma unroll
                         for (int mt = 0; mt < MT; ++mt) {
+                            if constexpr (kSplitHandoff) {
+                                if (!mbar_wait_sleep(&tempty[buf * MT + mt], tpar, abort_flag)) {
+                                    ok = false;
+                                    break;
+                                }
+                                tc_fence_after();
+                            }
 #pragma unroll
                             for (int ks = 0; ks < kChunkBytes / 32; ++ks)
                                 umma_u8(d0 + mt * BN, a_desc0 + mt * kBoxStep + 2 * ks, bd + 2 * ks, idesc,
                                         ks > 0 ? 1u : 0u);
                             if constexpr (kAug) umma_u8(d0 + mt * BN, a_aug_desc, bd_aug, idesc, 1u);
+                            if constexpr (kSplitHandoff) umma_commit(&tfull[buf * MT + mt]);
                         }
+                        if (!ok) break;
                         if (++s == S) {
                             s = 0;
                             ph ^= 1;
                         }
-                        umma_commit(&tfull[buf]);
+                        if constexpr (!kSplitHandoff) umma_commit(&tfull[buf]);
                     }
                 }
                 for (uint32_t j = 0; !lean && j < n_btiles && ok; ++j, ++acc_i) {
@@ -476,12 +492,16 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                         // follow. Clock reads only when profiling: every extra
                         // instruction in this thread delays the next MMAs.
                         if (!skip_tempty) {
-                            if (dbg) {
-                                const long long w0 = clock64();
-                                ok = mbar_wait(&tempty[buf], tpar ^ 1, abort_flag);
-                                c_tempty += clock64() - w0;
-                            } else {
-                                ok = mbar_wait(&tempty[buf], tpar ^ 1, abort_flag);
+                            // (split handoff: both M tiles' barriers of this buffer)
+                            for (int hm = 0; hm < (kSplitHandoff ? MT : 1) && ok; ++hm) {
+                                uint64_t* te = kSplitHandoff ? &tempty[buf * MT + hm] : &tempty[buf];
+                                if (dbg) {
+                                    const long long w0 = clock64();
+                                    ok = mbar_wait(te, tpar ^ 1, abort_flag);
+                                    c_tempty += clock64() - w0;
+                                } else {
+                                    ok = mbar_wait(te, tpar ^ 1, abort_flag);
+                                }
                             }
                             if (!ok) break;
                         }
@@ -506,7 +526,13 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                                 ph ^= 1;
                             }
                         }
-                        if (ok) umma_commit(&tfull[buf]);
+                        if (ok) {
+                            if constexpr (kSplitHandoff) {
+                                for (int hm = 0; hm < MT; ++hm) umma_commit(&tfull[buf * MT + hm]);
+                            } else {
+                                umma_commit(&tfull[buf]);
+                            }
+                        }
                         if (extra_commit) umma_commit(&bars[60]);  // profiling: one extra commit per tile
                     }
                 }
@@ -626,14 +652,14 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                 finish_norms(j);
                 __syncwarp();
                 const uint32_t buf = acc_i % NBUF;
-                const uint32_t hb = kPerMtBars ? mt : buf;  // handoff barrier
+                const uint32_t hb = kPerMtBars ? mt : (kSplitHandoff ? buf * MT + mt : buf);  // handoff barrier
                 const long long w0 = clock64();
                 ok = (p.debug_flags & 256u) ? mbar_wait_spin(&tfull[hb], (acc_i / NBUF) & 1, abort_flag)
                                                 : mbar_wait(&tfull[hb], (acc_i / NBUF) & 1, abort_flag);
                 c_tfull += clock64() - w0;
                 if (!ok) break;
                 tc_fence_after();
-                if (ew == (kPerMtBars ? 4 * (MT - 1) : 0) && lane == 0) *tiles_done = acc_i + 1;
+                if (ew == ((kPerMtBars || kSplitHandoff) ? 4 * (MT - 1) : 0) && lane == 0) *tiles_done = acc_i + 1;
                 const uint32_t tb = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + (buf * MT + mt) * BN +
                                     half * (BN / SPLIT);
                 constexpr int kCols = BN / SPLIT;  // columns of each tile this thread filters
