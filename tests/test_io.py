@@ -5,6 +5,7 @@ from __future__ import annotations
 
 import ctypes
 import subprocess
+import sys
 from pathlib import Path
 
 import numpy as np
@@ -169,3 +170,35 @@ def test_cli_rejects_bad_flags():
     assert r.returncode == 2 and "--metric must be" in r.stderr
     r = subprocess.run([str(CLI), "--k", "3"], capture_output=True, text=True)
     assert r.returncode == 2 and "missing required flag --dataset" in r.stderr
+
+
+def test_python_cli_arguments_and_relaunch():
+    from knng_gpu_b200.cli.__main__ import CliError, main, parse_args, relaunch_command
+
+    a = parse_args(["--dataset", "d.fvecs", "--k", "4"])
+    assert a.output == "d.fvecs.knng" and a.metric == "l2" and a.gpus == 1 and a.algorithm == "brute_force_gpu"
+    for bad in (["--dataset", "d.fvecs", "--k", "0"], ["--dataset", "d.fvecs", "--k", "3", "--metric", "cosine"],
+                ["--dataset", "d.fvecs", "--k", "3", "--gpus", "0"], ["--dataset", "d.fvecs", "--k", "x"],
+                ["--k", "3"]):
+        with pytest.raises(CliError):
+            parse_args(bad)
+    assert main(["--dataset", "d.fvecs", "--k", "3", "--metric", "cosine"]) == 2
+    cmd = relaunch_command(["--dataset", "d.fvecs", "--k", "3", "--gpus", "2"], 2, 29555)
+    assert cmd[1:3] == ["-m", "torch.distributed.run"] and "--nproc-per-node=2" in cmd
+    assert "--master-addr=127.0.0.1" in cmd and cmd[-6:] == ["--dataset", "d.fvecs", "--k", "3", "--gpus", "2"]
+
+
+@pytest.mark.gpu
+def test_python_cli_single_gpu(cuda_ok, tmp_path):
+    x = syn.generate(syn.KIND_UNIFORM_INT, 9, 600, 36)
+    for suffix, data in ((".bvecs", x.astype(np.uint8)), (".fvecs", x)):
+        p = tmp_path / f"d{suffix}"
+        kio.write_vecs(p, data)
+        out, gt = tmp_path / f"o{suffix}.knng", tmp_path / f"g{suffix}.gt"
+        r = subprocess.run([sys.executable, "-m", "knng_gpu_b200.cli", "--dataset", str(p), "--k", "7", "--output",
+                            str(out), "--ground-truth", str(gt)], capture_output=True, text=True, cwd=ROOT)
+        assert r.returncode == 0, r.stderr
+        ids, dists, m, a = kio.read_knng(out)
+        oi, od = oracle_knn(x, 7, 0)
+        assert np.array_equal(ids, oi) and np.array_equal(dists, od) and a == 1 and m == 0
+        assert kio.load_ground_truth(gt, x, 7, 0) is not None
