@@ -95,7 +95,7 @@ void knng_gpu_release_cached_buffers(void);
 /* ---- device-resident API (inputs already in HBM) ------------------------
  * All pointers are device pointers; `stream` is a cudaStream_t (NULL = the
  * legacy default stream). Nothing is allocated: the caller passes a
- * workspace of at least knng_gpu_workspace_bytes(n, d) bytes, 256-byte
+ * workspace of at least knng_gpu_workspace_bytes(n, d, k) bytes, 256-byte
  * aligned. Same semantics and output layout as knng_gpu_brute_force; the
  * call synchronises `stream` once (to read which path applies). */
 uint64_t knng_gpu_workspace_bytes(uint64_t n, uint64_t d, uint64_t k);
