@@ -48,8 +48,15 @@ inline void throw_on(knng_gpu_status st)
 }
 }  // namespace detail
 
+/// How to spread one build over the GPUs of this node (no counterpart in
+/// the reference, whose multi-node builder is src/dist/brute_force_mpi.cpp).
+struct Options {
+    int num_gpus = 1;   ///< devices 0..num_gpus-1, NCCL between them
+    bool ring = false;  ///< pass base blocks around a ring instead of replicating the base
+};
+
 template <Distance D>
-Knng brute_force_knn(const Dataset& ds, std::size_t k, D distance = D{})
+Knng brute_force_knn(const Dataset& ds, std::size_t k, D distance, const Options& opt)
 {
     (void)distance;
     if (ds.n == 0) {
@@ -63,9 +70,22 @@ Knng brute_force_knn(const Dataset& ds, std::size_t k, D distance = D{})
                                     ") must be <= ds.n - 1 (" + std::to_string(ds.n - 1) + ")");
     }
     Knng out(ds.n, k);
-    detail::throw_on(knng_gpu_brute_force(ds.data_ptr(), ds.n, ds.d, k, detail::metric_id<D>(),
-                                          out.neighbors.data(), out.distances.data(), nullptr));
+    if (opt.num_gpus > 1 || opt.ring) {
+        detail::throw_on(knng_gpu_brute_force_multi(ds.data_ptr(), ds.n, ds.d, k, detail::metric_id<D>(),
+                                                    opt.num_gpus, opt.ring ? 1 : 0, out.neighbors.data(),
+                                                    out.distances.data(), nullptr));
+    } else {
+        detail::throw_on(knng_gpu_brute_force(ds.data_ptr(), ds.n, ds.d, k, detail::metric_id<D>(),
+                                              out.neighbors.data(), out.distances.data(), nullptr));
+    }
     return out;
+}
+
+/// The reference's signature: one GPU (the current device).
+template <Distance D>
+Knng brute_force_knn(const Dataset& ds, std::size_t k, D distance = D{})
+{
+    return brute_force_knn(ds, k, distance, Options{});
 }
 
 }  // namespace knng::gpu

@@ -59,6 +59,7 @@ typedef struct {
     float total_ms;           /* whole call, device time */
     uint32_t kernel_launches; /* kernels this call launched */
     float f32_err_ratio;      /* fp32 path: max |approximate - exact| / proof margin seen (< 1) */
+    float tc_ms;              /* the tensor-core kernel alone (device time; the roofline's denominator) */
 } knng_gpu_stats;
 
 /* Message of the last failure on this thread ("" if none). */
@@ -124,7 +125,7 @@ knng_gpu_status knng_gpu_brute_force_device(const float* d_data, uint64_t n, uin
  *   d_q_norms / d_b_norms arguments below.
  * knng_gpu_knn_u8: queries are packed rows [q_begin, q_begin+q_count) of the
  *   base; results for query row i go to row i of d_ids/d_dists (q_count x k).
- *   d_scratch: >= knng_gpu_knn_scratch_bytes(q_count) bytes.
+ *   d_scratch: >= knng_gpu_knn_scratch_bytes(q_count, k) bytes, 256-byte aligned.
  * knng_gpu_knn_f32: any fp32 data: bf16x3 tensor-core candidate filter over
  *   all n rows, exact re-rank with the reference's arithmetic and a proven
  *   error bound, exact kernel for rows the bound cannot certify.
@@ -137,7 +138,7 @@ knng_gpu_status knng_gpu_pack_u8(const float* d_x, uint64_t rows, uint64_t d, ui
  *   already bytes (row r at d_rows + r * row_stride, row_stride >= d). */
 knng_gpu_status knng_gpu_pack_u8_bytes(const uint8_t* d_rows, uint64_t rows, uint64_t d, uint64_t row_stride,
                                        uint8_t* d_packed, int32_t* d_norms, void* stream);
-uint64_t knng_gpu_knn_scratch_bytes(uint64_t q_count);
+uint64_t knng_gpu_knn_scratch_bytes(uint64_t q_count, uint64_t k);
 knng_gpu_status knng_gpu_knn_u8(const uint8_t* d_packed, const int32_t* d_norms, uint64_t n, uint64_t d,
                                 uint64_t q_begin, uint64_t q_count, uint64_t k, int metric, uint32_t* d_ids,
                                 float* d_dists, void* d_scratch, uint64_t scratch_bytes, void* stream,
@@ -147,7 +148,7 @@ knng_gpu_status knng_gpu_knn_u8(const uint8_t* d_packed, const int32_t* d_norms,
  *   row r is b_id0 + r, query row i is q_id0 + i; with exclude_self a query
  *   never returns its own id (src/dist/brute_force_mpi.cpp:80-82 excludes by
  *   global index the same way). Needs n_b >= k (+1 with exclude_self).
- *   d_scratch: >= knng_gpu_knn_scratch_bytes(n_q) bytes.
+ *   d_scratch: >= knng_gpu_knn_scratch_bytes(n_q, k) bytes, 256-byte aligned.
  * knng_gpu_merge_topk: row-wise merge of two sorted k-lists into the k best
  *   by (distance, id), the TopK order (include/knng/top_k.hpp:56-72); merges
  *   the per-block results of a ring pass. */
@@ -160,6 +161,27 @@ knng_gpu_status knng_gpu_merge_topk(const uint32_t* d_a_ids, const float* d_a_di
                                     const float* d_b_dists, uint64_t rows, uint64_t k, uint32_t* d_out_ids,
                                     float* d_out_dists, void* stream);
 uint64_t knng_gpu_knn_f32_scratch_bytes(uint64_t n, uint64_t d, uint64_t q_count, uint64_t k);
+/* knng_gpu_knn_f32_sets: fp32 query rows against separate fp32 base rows
+ *   (cross-set KNN: the batched query != base search the reference's recall
+ *   harness needs, src/bench/recall.cpp and src/bench/ground_truth.cpp).
+ *   Same exactness as knng_gpu_knn_f32 (bf16x3 tensor-core filter, exact
+ *   re-rank with the reference's arithmetic, exact kernel for rows the bound
+ *   cannot certify); ids are global as in knng_gpu_knn_u8_sets. Needs
+ *   n_b >= k (+1 with exclude_self). d_scratch: >=
+ *   knng_gpu_knn_f32_sets_scratch_bytes(n_q, n_b, d, k, exclude_self) bytes,
+ *   256-byte aligned. */
+uint64_t knng_gpu_knn_f32_sets_scratch_bytes(uint64_t n_q, uint64_t n_b, uint64_t d, uint64_t k, int exclude_self);
+knng_gpu_status knng_gpu_knn_f32_sets(const float* d_q, uint64_t n_q, uint64_t q_id0, const float* d_b, uint64_t n_b,
+                                      uint64_t b_id0, uint64_t d, uint64_t k, int metric, int exclude_self,
+                                      uint32_t* d_ids, float* d_dists, void* d_scratch, uint64_t scratch_bytes,
+                                      void* stream, knng_gpu_stats* stats);
+/* knng_gpu_recall_at_k: recall@k of an approximate graph against the true
+ *   graph, both n x k device id arrays -- knng::bench::recall_at_k
+ *   (src/bench/recall.cpp:79-96): the fraction of true neighbours found,
+ *   where a repeated approximate id counts once (:52-77); 1.0 for n == 0.
+ *   d_counter: 8 device bytes of scratch. Synchronises `stream`. */
+knng_gpu_status knng_gpu_recall_at_k(const uint32_t* d_approx, const uint32_t* d_truth, uint64_t n, uint64_t k,
+                                     void* d_counter, void* stream, double* recall);
 knng_gpu_status knng_gpu_knn_f32(const float* d_x, uint64_t n, uint64_t d, uint64_t q_begin, uint64_t q_count,
                                  uint64_t k, int metric, uint32_t* d_ids, float* d_dists, void* d_scratch,
                                  uint64_t scratch_bytes, void* stream, knng_gpu_stats* stats);
@@ -176,17 +198,76 @@ knng_gpu_status knng_gpu_knn_f32(const float* d_x, uint64_t n, uint64_t d, uint6
  * the process exits). Limits and caveats:
  *   - q_count must be <= KNNG_GPU_NOALLOC_MAX_QUERIES, else
  *     KNNG_GPU_INVALID_ARGUMENT;
- *   - the first call on a device looks up the array's device address (once
- *     per device, with that device current); make that first call before any
- *     stream capture;
+ *   - the first call in a CUDA context looks up the array's address in that
+ *     context (cudaGetSymbolAddress, with the context current) and caches it
+ *     per context; knng_gpu_release_cached_buffers empties that cache (call
+ *     it after cudaDeviceReset);
  *   - all calls share the one array: calls that overlap on the GPU (other
  *     streams, other host threads) race and must be serialised by the caller.
  * The call allocates nothing: no cudaMalloc/cudaFree and no allocating
- * library routine. */
+ * library routine; it runs the single-CTA kernel (the array has no room for
+ * the partial lists of the CTA-pair kernel) and records no timing events, so
+ * the *_ms fields of `stats` are 0. Like every entry point here it ends by
+ * synchronising `stream` once, to read the fallback count and the error
+ * word of the bounded device waits. */
 #define KNNG_GPU_NOALLOC_MAX_QUERIES (1u << 20)
 knng_gpu_status knng_gpu_knn_u8_noalloc(const uint8_t* d_packed, const int32_t* d_norms, uint64_t n, uint64_t d,
                                         uint64_t q_begin, uint64_t q_count, uint64_t k, int metric, uint32_t* d_ids,
                                         float* d_dists, void* stream, knng_gpu_stats* stats);
+
+/* ---- multi-GPU builds (NCCL) ---------------------------------------------
+ * The reference's distributed build (src/dist/brute_force_mpi.cpp:36-203 over
+ * MPI, sharded by include/knng/dist/sharded_dataset.hpp:145-155) as NCCL
+ * ranks, one GPU each. Two ways to drive it:
+ *
+ * (1) one process per GPU (e.g. torchrun): rank 0 calls
+ *     knng_gpu_nccl_unique_id, hands the knng_gpu_nccl_id_bytes() bytes to
+ *     every rank by any channel, and every rank calls knng_gpu_comm_create
+ *     with its device current, then knng_gpu_brute_force_sharded for each
+ *     build. d_rows holds the rank's rows [begin, begin + count) given by
+ *     knng_gpu_shard_rows. Rank 0 receives the whole n x k graph in
+ *     d_ids/d_dists (device pointers; other ranks may pass NULL).
+ * (2) one process driving num_gpus GPUs (devices 0..num_gpus-1):
+ *     knng_gpu_brute_force_multi with host buffers, like
+ *     knng_gpu_brute_force; communicators, streams and device buffers are
+ *     kept between calls until knng_gpu_release_multi.
+ *
+ * mode 0 (replicate): the packed base is all-gathered to every GPU and each
+ *   rank searches its compute_shard query rows against it; any data.
+ * mode 1 (ring): the base stays sharded; blocks are passed around the ring
+ *   (the reference's MPI_Sendrecv ring, brute_force_mpi.cpp:71-124) while the
+ *   kernel searches the current block, and the per-query lists are merged by
+ *   (distance, id). Integer-valued data in [0, 255] only, and at least k + 1
+ *   rows per rank.
+ * Every rank must make the same calls with the same arguments. Output is
+ * identical to knng_gpu_brute_force for every rank count and mode. */
+uint64_t knng_gpu_nccl_id_bytes(void);
+knng_gpu_status knng_gpu_nccl_unique_id(void* id_out);
+knng_gpu_status knng_gpu_comm_create(const void* id, int world, int rank, void** comm_out);
+void knng_gpu_comm_destroy(void* comm);
+void knng_gpu_shard_rows(uint64_t n, int world, int rank, int mode, uint64_t* begin, uint64_t* count);
+uint64_t knng_gpu_sharded_workspace_bytes(uint64_t n, uint64_t d, uint64_t k, int world, int mode);
+knng_gpu_status knng_gpu_brute_force_sharded(const float* d_rows, uint64_t n, uint64_t d, uint64_t k, int metric,
+                                             int mode, void* comm, uint32_t* d_ids, float* d_dists,
+                                             void* d_workspace, uint64_t workspace_bytes, void* stream,
+                                             knng_gpu_stats* stats);
+/* Device time of the phases of the last sharded build on this rank (filled
+ * when that build had non-NULL stats): pack, base exchange, search, fp32
+ * exchange + search, gather to rank 0, total. */
+knng_gpu_status knng_gpu_comm_phase_ms(void* comm, float* out6);
+knng_gpu_status knng_gpu_brute_force_multi(const float* data, uint64_t n, uint64_t d, uint64_t k, int metric,
+                                           int num_gpus, int mode, uint32_t* ids, float* dists,
+                                           knng_gpu_stats* stats);
+void knng_gpu_release_multi(void);
+
+/* ---- test hook -----------------------------------------------------------
+ * Runs one small build whose device-side waits give up after
+ * `wait_limit_cycles` clock cycles while the kernel's producer withholds one
+ * arrival on purpose. Returns KNNG_GPU_TIMEOUT when the bounded waits work
+ * (the kernel unwinds, frees its TMEM and the CUDA context stays usable).
+ * Allocates and frees its own small buffers. No counterpart in the
+ * reference, whose code has no device waits. */
+knng_gpu_status knng_gpu_selftest_bounded_wait(uint64_t wait_limit_cycles);
 
 #ifdef __cplusplus
 }

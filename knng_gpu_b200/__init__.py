@@ -13,10 +13,13 @@ from .api import (  # noqa: F401
     NegativeInnerProduct,
     brute_force_knn,
     brute_force_knn_device,
+    brute_force_knn_multi,
     brute_force_knn_u8,
     device_count,
     knn_f32,
     knn_f32_scratch_bytes,
+    knn_f32_sets,
+    knn_f32_sets_scratch_bytes,
     knn_scratch_bytes,
     knn_u8,
     knn_u8_sets,
@@ -24,5 +27,6 @@ from .api import (  # noqa: F401
     pack_u8,
     pack_u8_bytes,
     padded_dim,
+    recall_at_k,
     workspace_bytes,
 )

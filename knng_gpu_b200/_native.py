@@ -34,6 +34,20 @@ GPU_SYMBOLS = (
     "knng_gpu_knn_u8_noalloc",
     "knng_gpu_brute_force_u8",
     "knng_gpu_pack_u8_bytes",
+    "knng_gpu_selftest_bounded_wait",
+    "knng_gpu_nccl_id_bytes",
+    "knng_gpu_nccl_unique_id",
+    "knng_gpu_comm_create",
+    "knng_gpu_comm_destroy",
+    "knng_gpu_shard_rows",
+    "knng_gpu_sharded_workspace_bytes",
+    "knng_gpu_brute_force_sharded",
+    "knng_gpu_comm_phase_ms",
+    "knng_gpu_brute_force_multi",
+    "knng_gpu_release_multi",
+    "knng_gpu_knn_f32_sets_scratch_bytes",
+    "knng_gpu_knn_f32_sets",
+    "knng_gpu_recall_at_k",
 )
 
 
@@ -49,6 +63,7 @@ class KnngGpuStats(ctypes.Structure):
         ("total_ms", c_float),
         ("kernel_launches", c_uint32),
         ("f32_err_ratio", c_float),
+        ("tc_ms", c_float),
     ]
 
     def as_dict(self) -> dict:
@@ -85,7 +100,27 @@ def gpu_lib() -> ctypes.CDLL:
             ),
             "knng_gpu_padded_dim": (c_uint64, [c_uint64]),
             "knng_gpu_pack_u8": (c_int, [c_void_p, c_uint64, c_uint64, c_void_p, c_void_p, c_void_p, c_void_p]),
-            "knng_gpu_knn_scratch_bytes": (c_uint64, [c_uint64]),
+            "knng_gpu_knn_scratch_bytes": (c_uint64, [c_uint64, c_uint64]),
+            "knng_gpu_selftest_bounded_wait": (c_int, [c_uint64]),
+            "knng_gpu_nccl_id_bytes": (c_uint64, []),
+            "knng_gpu_nccl_unique_id": (c_int, [c_void_p]),
+            "knng_gpu_comm_create": (c_int, [c_void_p, c_int, c_int, POINTER(c_void_p)]),
+            "knng_gpu_comm_destroy": (None, [c_void_p]),
+            "knng_gpu_shard_rows": (None, [c_uint64, c_int, c_int, c_int, POINTER(c_uint64), POINTER(c_uint64)]),
+            "knng_gpu_sharded_workspace_bytes": (c_uint64, [c_uint64, c_uint64, c_uint64, c_int, c_int]),
+            "knng_gpu_brute_force_sharded": (
+                c_int, [c_void_p, c_uint64, c_uint64, c_uint64, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                        c_void_p, c_uint64, c_void_p, st]),
+            "knng_gpu_comm_phase_ms": (c_int, [c_void_p, POINTER(c_float)]),
+            "knng_gpu_brute_force_multi": (
+                c_int, [c_void_p, c_uint64, c_uint64, c_uint64, c_int, c_int, c_int, c_void_p, c_void_p, st]),
+            "knng_gpu_release_multi": (None, []),
+            "knng_gpu_knn_f32_sets_scratch_bytes": (c_uint64, [c_uint64, c_uint64, c_uint64, c_uint64, c_int]),
+            "knng_gpu_knn_f32_sets": (
+                c_int, [c_void_p, c_uint64, c_uint64, c_void_p, c_uint64, c_uint64, c_uint64, c_uint64, c_int, c_int,
+                        c_void_p, c_void_p, c_void_p, c_uint64, c_void_p, st]),
+            "knng_gpu_recall_at_k": (c_int, [c_void_p, c_void_p, c_uint64, c_uint64, c_void_p, c_void_p,
+                                             POINTER(ctypes.c_double)]),
             "knng_gpu_brute_force_u8": (
                 c_int, [c_void_p, c_uint64, c_uint64, c_uint64, c_uint64, c_int, c_void_p, c_void_p, st]),
             "knng_gpu_pack_u8_bytes": (c_int, [c_void_p, c_uint64, c_uint64, c_uint64, c_void_p, c_void_p, c_void_p]),
@@ -131,6 +166,9 @@ def synth_lib() -> ctypes.CDLL:
         lib.knng_synth_generate.restype = c_int
         lib.knng_synth_generate.argtypes = [c_int, c_uint64, c_uint64, c_uint64, c_void_p, c_uint64, c_float,
                                             c_float, c_void_p]
+        lib.knng_synth_generate_rows.restype = c_int
+        lib.knng_synth_generate_rows.argtypes = [c_int, c_uint64, c_uint64, c_uint64, c_uint64, c_void_p, c_uint64,
+                                                 c_float, c_float, c_void_p]
         lib.knng_dataset_hash.restype = c_uint64
         lib.knng_dataset_hash.argtypes = [c_void_p, c_uint64, c_uint64]
         lib.knng_synth_sample_ids.restype = c_int

@@ -169,6 +169,27 @@ def brute_force_knn_u8(rows: np.ndarray, k: int, distance=L2Squared(), d: int | 
     return Knng(n, k, ids[: n * k], dists[: n * k], stats.as_dict())
 
 
+def brute_force_knn_multi(ds: Dataset | np.ndarray, k: int, distance=L2Squared(), num_gpus: int = 1,
+                          ring: bool = False) -> Knng:
+    """:func:`brute_force_knn` on ``num_gpus`` GPUs of this process (devices
+    0..num_gpus-1, NCCL between them): query rows sharded like the reference's
+    distributed build, the base all-gathered (or ring-passed with ``ring``),
+    the graph gathered on GPU 0. Same output as :func:`brute_force_knn`."""
+    if isinstance(ds, np.ndarray):
+        ds = Dataset.from_array(ds)
+    if k < 0:
+        raise InvalidArgument("knng::gpu::brute_force_knn: k must be > 0")
+    data = np.ascontiguousarray(ds.data, dtype=np.float32)
+    n, d = int(ds.n), int(ds.d)
+    ids = np.empty(max(n * k, 1), dtype=np.uint32)
+    dists = np.empty(max(n * k, 1), dtype=np.float32)
+    stats = KnngGpuStats()
+    check(gpu_lib().knng_gpu_brute_force_multi(
+        data.ctypes.data if data.size else None, n, d, k, _metric_id(distance), num_gpus, 1 if ring else 0,
+        ids.ctypes.data, dists.ctypes.data, ctypes.byref(stats)))
+    return Knng(n, k, ids[: n * k], dists[: n * k], stats.as_dict())
+
+
 # ---------------------------------------------------------------- device API
 def _ptr(t) -> int | None:
     return None if t is None else int(t.data_ptr())
@@ -235,8 +256,8 @@ def pack_u8_bytes(rows, packed, norms, d: int | None = None, stream=None) -> Non
                                            _stream_handle(stream)))
 
 
-def knn_scratch_bytes(q_count: int) -> int:
-    return int(gpu_lib().knng_gpu_knn_scratch_bytes(q_count))
+def knn_scratch_bytes(q_count: int, k: int) -> int:
+    return int(gpu_lib().knng_gpu_knn_scratch_bytes(q_count, k))
 
 
 def knn_u8(packed, norms, n: int, d: int, q_begin: int, q_count: int, k: int, distance, out_ids, out_dists,
@@ -280,6 +301,44 @@ def knn_f32(x, n: int, d: int, q_begin: int, q_count: int, k: int, distance, out
                                      _ptr(out_dists), _ptr(scratch), scratch.numel(), _stream_handle(stream),
                                      ctypes.byref(stats)))
     return stats.as_dict()
+
+
+def knn_f32_sets_scratch_bytes(n_q: int, n_b: int, d: int, k: int, exclude_self: bool = False) -> int:
+    return int(gpu_lib().knng_gpu_knn_f32_sets_scratch_bytes(n_q, n_b, d, k, int(exclude_self)))
+
+
+def knn_f32_sets(q, q_id0: int, b, b_id0: int, k: int, distance, exclude_self: bool, out_ids, out_dists,
+                 scratch=None, stream=None) -> dict:
+    """Exact KNN of fp32 query rows ``q`` (CUDA (n_q, d)) against separate fp32
+    base rows ``b`` (CUDA (n_b, d)) with global ids; the fp32 path of
+    :func:`knn_f32` for two sets."""
+    import torch
+
+    n_q, d = q.shape
+    n_b = b.shape[0]
+    if scratch is None:
+        scratch = torch.empty(knn_f32_sets_scratch_bytes(n_q, n_b, d, k, exclude_self), dtype=torch.uint8,
+                              device=q.device)
+    stats = KnngGpuStats()
+    check(gpu_lib().knng_gpu_knn_f32_sets(_ptr(q), n_q, q_id0, _ptr(b), n_b, b_id0, d, k, _metric_id(distance),
+                                          int(exclude_self), _ptr(out_ids), _ptr(out_dists), _ptr(scratch),
+                                          scratch.numel(), _stream_handle(stream), ctypes.byref(stats)))
+    return stats.as_dict()
+
+
+def recall_at_k(approx_ids, truth_ids, stream=None) -> float:
+    """knng::bench::recall_at_k (src/bench/recall.cpp:79-96) on the GPU: both
+    arguments are CUDA (n, k) id tensors; a repeated approximate id counts once."""
+    import torch
+
+    if approx_ids.shape != truth_ids.shape:
+        raise InvalidArgument("knng::bench::recall: approx and truth shapes differ")
+    n, k = approx_ids.shape
+    counter = torch.empty(1, dtype=torch.int64, device=approx_ids.device)
+    out = ctypes.c_double()
+    check(gpu_lib().knng_gpu_recall_at_k(_ptr(approx_ids.contiguous()), _ptr(truth_ids.contiguous()), n, k,
+                                         _ptr(counter), _stream_handle(stream), ctypes.byref(out)))
+    return float(out.value)
 
 
 def device_count() -> int:

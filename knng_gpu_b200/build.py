@@ -39,7 +39,7 @@ def build_gpu(verbose: bool = False, force: bool = False) -> Path:
     if force or _stale(out, srcs):
         tmp = out.with_suffix(".so.tmp")
         _run([NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "-shared",
-              f"-I{ROOT / 'include'}", "-o", str(tmp), str(CSRC / "knng_gpu.cu")], verbose)
+              f"-I{ROOT / 'include'}", "-o", str(tmp), str(CSRC / "knng_gpu.cu"), "-lnccl"], verbose)
         tmp.replace(out)
     return out
 

@@ -5,10 +5,11 @@ The flags, messages and output of the reference's ``build_knng``
 l2|inner_product] [--algorithm brute_force_gpu|brute_force] [--output PATH]
 [--ground-truth PATH]``, plus ``--gpus N``. One GPU calls the C ABI directly
 (``.bvecs`` bytes go to the u8 entry point without a float copy). With N > 1
-the command re-launches itself as N processes (one per GPU, torch.distributed
-over NCCL, rendezvous on 127.0.0.1); every rank reads the dataset, packs and
-searches its query shard with :class:`~knng_gpu_b200.distributed.ShardedBuilder`,
-and rank 0 writes the ``.knng`` file (and the ground-truth cache).
+this process drives GPUs 0..N-1 through knng_gpu_brute_force_multi (NCCL
+inside the library). Started under torchrun instead (``relaunch_command``
+gives that command line), every rank reads the dataset, packs and searches
+its query shard with :class:`~knng_gpu_b200.distributed.ShardedBuilder`, and
+rank 0 writes the ``.knng`` file (and the ground-truth cache).
 """
 from __future__ import annotations
 
@@ -99,7 +100,13 @@ def run_single(a) -> int:
     _log(f"loaded n={n} d={d}")
     metric = 0 if a.metric == "l2" else 1
     _log(f"building k={a.k} metric={a.metric} algorithm={a.algorithm}")
-    g = kg.brute_force_knn_u8(x, a.k, metric) if x.dtype == np.uint8 else kg.brute_force_knn(x, a.k, metric)
+    if a.gpus > 1:
+        # One process drives the GPUs (NCCL inside the library).
+        g = kg.brute_force_knn_multi(np.asarray(x, np.float32), a.k, metric, num_gpus=a.gpus)
+    elif x.dtype == np.uint8:
+        g = kg.brute_force_knn_u8(x, a.k, metric)
+    else:
+        g = kg.brute_force_knn(x, a.k, metric)
     _write_outputs(a, x, g.neighbors.reshape(n, a.k), g.distances.reshape(n, a.k), metric)
     _log("done")
     return 0
@@ -147,8 +154,6 @@ def main(argv: list[str] | None = None) -> int:
     try:
         if "RANK" in os.environ and int(os.environ.get("WORLD_SIZE", "1")) > 1:
             return run_rank(a)
-        if a.gpus > 1:
-            return subprocess.call(relaunch_command(argv, a.gpus, _free_port()))
         return run_single(a)
     except Exception as e:  # the reference prints the message and exits 1
         print(f"build_knng_gpu: {e}", file=sys.stderr)

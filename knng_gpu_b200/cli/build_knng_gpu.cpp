@@ -4,7 +4,7 @@
 //
 //   build_knng_gpu --dataset PATH --k N [--metric l2|inner_product]
 //                  [--algorithm brute_force_gpu|brute_force] [--output PATH]
-//                  [--ground-truth PATH] [--device I]
+//                  [--ground-truth PATH] [--device I] [--gpus N]
 //
 // .fvecs datasets are read as in the reference; .bvecs datasets (u8 rows) are
 // read directly and feed the exact u8 tensor-core path. The header's
@@ -44,6 +44,7 @@ constexpr std::string_view kUsage =
     "  --output PATH         Output .knng path (default: <dataset>.knng)\n"
     "  --ground-truth PATH   Also write a ground-truth cache file\n"
     "  --device I            CUDA device (default 0)\n"
+    "  --gpus N              Build on GPUs 0..N-1 of this node (default 1)\n"
     "  --help                Print this message and exit\n";
 
 struct Args {
@@ -52,6 +53,7 @@ struct Args {
     std::string metric = "l2";
     std::string algorithm = "brute_force_gpu";
     int device = 0;
+    int gpus = 1;
 };
 
 std::uint64_t parse_size(const std::string& s, const char* flag)
@@ -63,42 +65,67 @@ std::uint64_t parse_size(const std::string& s, const char* flag)
     return v;
 }
 
+// Every accepted flag, in the order its value is checked: the reference's
+// flag names and error messages (tools/build_knng.cpp:100-179), plus
+// --ground-truth, --device and --gpus.
+struct FlagSpec {
+    const char* name;
+    bool required;
+    void (*apply)(Args&, const std::string&);
+};
+
+const FlagSpec kFlags[] = {
+    {"dataset", true, [](Args& a, const std::string& v) { a.dataset = v; }},
+    {"k", true, [](Args& a, const std::string& v) { a.k = parse_size(v, "--k"); }},
+    {"metric", false, [](Args& a, const std::string& v) { a.metric = v; }},
+    {"algorithm", false, [](Args& a, const std::string& v) { a.algorithm = v; }},
+    {"output", false, [](Args& a, const std::string& v) { a.output = v; }},
+    {"ground-truth", false, [](Args& a, const std::string& v) { a.ground_truth = v; }},
+    {"device", false, [](Args& a, const std::string& v) { a.device = static_cast<int>(parse_size(v, "--device")); }},
+    {"gpus", false, [](Args& a, const std::string& v) { a.gpus = static_cast<int>(parse_size(v, "--gpus")); }},
+};
+
+const FlagSpec* find_flag(const std::string& name)
+{
+    for (const FlagSpec& f : kFlags)
+        if (name == f.name) return &f;
+    return nullptr;
+}
+
+// argv -> Args in three steps: split into (--name, value) pairs, apply the
+// spec table (a repeated flag keeps its last value), then check the values
+// against each other. nullopt: --help.
 std::optional<Args> parse_args(int argc, char** argv)
 {
-    Args a;
-    std::map<std::string, std::string> values;
-    for (int i = 1; i < argc;) {
-        const std::string_view s = argv[i];
-        if (s == "--help" || s == "-h") return std::nullopt;
-        if (s.substr(0, 2) != "--") throw std::invalid_argument("unexpected positional argument: '" + std::string{s} + "'");
-        if (i + 1 >= argc) throw std::invalid_argument("flag '" + std::string{s} + "' requires a value");
-        values[std::string{s.substr(2)}] = argv[i + 1];
-        i += 2;
+    std::vector<std::pair<std::string, std::string>> given;
+    for (int i = 1; i < argc; i += 2) {
+        const std::string tok = argv[i];
+        if (tok == "--help" || tok == "-h") return std::nullopt;
+        if (tok.rfind("--", 0) != 0) throw std::invalid_argument("unexpected positional argument: '" + tok + "'");
+        if (i + 1 >= argc) throw std::invalid_argument("flag '" + tok + "' requires a value");
+        given.emplace_back(tok.substr(2), argv[i + 1]);
     }
-    auto take = [&](const std::string& key, bool required) -> std::optional<std::string> {
-        auto it = values.find(key);
-        if (it == values.end()) {
-            if (required) throw std::invalid_argument("missing required flag --" + key);
-            return std::nullopt;
-        }
-        std::string v = it->second;
-        values.erase(it);
-        return v;
-    };
-    a.dataset = *take("dataset", true);
-    a.k = parse_size(*take("k", true), "--k");
-    if (auto m = take("metric", false)) a.metric = *m;
-    if (auto al = take("algorithm", false)) a.algorithm = *al;
-    if (auto o = take("output", false)) a.output = *o;
-    if (auto g = take("ground-truth", false)) a.ground_truth = *g;
-    if (auto dv = take("device", false)) a.device = static_cast<int>(parse_size(*dv, "--device"));
-    if (!values.empty()) throw std::invalid_argument("unknown flag --" + values.begin()->first);
+    Args a;
+    for (const FlagSpec& f : kFlags) {
+        const std::string* value = nullptr;
+        for (const auto& [name, v] : given)
+            if (name == f.name) value = &v;
+        if (value)
+            f.apply(a, *value);
+        else if (f.required)
+            throw std::invalid_argument(std::string{"missing required flag --"} + f.name);
+    }
+    std::string unknown;  // the alphabetically first unknown flag is reported
+    for (const auto& [name, v] : given)
+        if (!find_flag(name) && (unknown.empty() || name < unknown)) unknown = name;
+    if (!unknown.empty()) throw std::invalid_argument("unknown flag --" + unknown);
     if (a.k == 0) throw std::invalid_argument("--k must be > 0");
     if (a.output.empty()) a.output = a.dataset + ".knng";
     if (a.metric != "l2" && a.metric != "inner_product")
         throw std::invalid_argument("--metric must be 'l2' or 'inner_product', got '" + a.metric + "'");
     if (a.algorithm != "brute_force_gpu" && a.algorithm != "brute_force")
         throw std::invalid_argument("--algorithm must be 'brute_force_gpu' or 'brute_force', got '" + a.algorithm + "'");
+    if (a.gpus < 1) throw std::invalid_argument("--gpus must be > 0");
     return a;
 }
 
@@ -136,7 +163,8 @@ int main(int argc, char** argv)
         else
             knng_files::read_vecs<float>(args.dataset, x, n, d);
         std::cerr << "build_knng_gpu: loaded n=" << n << " d=" << d << '\n';
-        if (cudaSetDevice(args.device) != cudaSuccess) throw std::runtime_error("cudaSetDevice failed");
+        if (args.gpus == 1 && cudaSetDevice(args.device) != cudaSuccess)
+            throw std::runtime_error("cudaSetDevice failed");
         const std::uint32_t metric = args.metric == "l2" ? KNNG_METRIC_L2_SQUARED : KNNG_METRIC_NEGATIVE_INNER_PRODUCT;
         std::cerr << "build_knng_gpu: building k=" << args.k << " metric=" << args.metric
                   << " algorithm=" << args.algorithm << '\n';
@@ -146,11 +174,18 @@ int main(int argc, char** argv)
         g.ids.resize(n * args.k);
         g.dists.resize(n * args.k);
         knng_gpu_stats stats{};
-        const knng_gpu_status st =
-            bytes ? knng_gpu_brute_force_u8(raw.data(), n, d, d, args.k, static_cast<int>(metric), g.ids.data(),
-                                            g.dists.data(), &stats)
-                  : knng_gpu_brute_force(x.data(), n, d, args.k, static_cast<int>(metric), g.ids.data(),
-                                         g.dists.data(), &stats);
+        knng_gpu_status st;
+        if (args.gpus > 1) {
+            // Devices 0..gpus-1 from this process (NCCL inside the library).
+            if (bytes) x.assign(raw.begin(), raw.end());
+            st = knng_gpu_brute_force_multi(x.data(), n, d, args.k, static_cast<int>(metric), args.gpus, 0,
+                                            g.ids.data(), g.dists.data(), &stats);
+        } else {
+            st = bytes ? knng_gpu_brute_force_u8(raw.data(), n, d, d, args.k, static_cast<int>(metric), g.ids.data(),
+                                                 g.dists.data(), &stats)
+                       : knng_gpu_brute_force(x.data(), n, d, args.k, static_cast<int>(metric), g.ids.data(),
+                                              g.dists.data(), &stats);
+        }
         if (st != KNNG_GPU_OK) throw std::runtime_error(knng_gpu_last_error());
         std::cerr << "build_knng_gpu: device time " << stats.total_ms << " ms (path "
                   << (stats.path == KNNG_PATH_U8_TENSOR ? "u8 tensor" : "fp32 tensor") << ")\n";

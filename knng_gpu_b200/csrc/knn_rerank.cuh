@@ -94,16 +94,19 @@ __global__ void __launch_bounds__(256) split_bf16_kernel(const float* __restrict
 }
 
 struct RerankParams {
-    const float* x;            // original rows (the reference's data)
+    const float* x;            // base rows (the reference's data); base row r has id base_id0 + r
+    const float* qx;           // query rows; query i has id query_id0 + i
     uint64_t d;
-    uint64_t n;
-    uint32_t q_begin;          // query i is row q_begin + i
+    uint64_t n_b;              // base rows
+    uint32_t base_id0;
+    uint32_t query_id0;
+    uint32_t exclude_self;
     uint32_t n_queries;
     uint32_t c;                // candidates per row
     uint32_t k;
     const uint32_t* cand_ids;  // n_queries x c, ascending approximate key
     const int32_t* cand_keys;  // ordered approximate keys
-    const float* norms;        // |x'|^2 per row (centred for L2)
+    const float* q_norms;      // |q'|^2 per query row (centred for L2)
     const unsigned int* max_norm_bits;
     double gamma;              // eps = gamma * (|q'| + R)^2 (L2) or gamma * |q| R (IP)
     uint32_t* out_ids;         // n_queries x k
@@ -128,8 +131,11 @@ __global__ void __launch_bounds__(32 * kRerankWarps) rerank_kernel(const RerankP
     const uint64_t warp0 = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = (static_cast<uint64_t>(gridDim.x) * blockDim.x) >> 5;
     for (uint64_t qi = warp0; qi < p.n_queries; qi += nwarps) {
-        const uint64_t q = p.q_begin + qi;
-        const float* qr = p.x + q * p.d;
+        const float* qr = p.qx + qi * p.d;
+        const uint32_t qid = p.query_id0 + static_cast<uint32_t>(qi);
+        // Base rows this query can see: all, minus itself when excluded.
+        const uint64_t eligible =
+            p.n_b - ((p.exclude_self && qid >= p.base_id0 && qid - p.base_id0 < p.n_b) ? 1 : 0);
         int32_t key[CPL];
         uint32_t id[CPL];
         float dist[CPL];
@@ -145,8 +151,9 @@ __global__ void __launch_bounds__(32 * kRerankWarps) rerank_kernel(const RerankP
                     qtile[wib][lane] = col < p.d ? qr[col] : 0.0f;
                     for (int r = 0; r < 32; ++r) {
                         const uint32_t rid = __shfl_sync(0xffffffffu, id[t], r);
-                        tile[wib][r][lane] = (rid != UINT32_MAX && col < p.d) ? p.x[static_cast<uint64_t>(rid) * p.d + col]
-                                                                           : 0.0f;
+                        tile[wib][r][lane] = (rid != UINT32_MAX && col < p.d)
+                                                 ? p.x[static_cast<uint64_t>(rid - p.base_id0) * p.d + col]
+                                                 : 0.0f;
                     }
                     __syncwarp();
                     const int cnt = p.d - d0 < 32 ? static_cast<int>(p.d - d0) : 32;
@@ -180,7 +187,7 @@ __global__ void __launch_bounds__(32 * kRerankWarps) rerank_kernel(const RerankP
         }
         // Diagnostic: how close the observed filter error comes to eps.
         {
-            const float qn = p.norms[q];
+            const float qn = p.q_norms[qi];
             const double R = static_cast<double>(__uint_as_float(*p.max_norm_bits));
             const double sq = sqrt(static_cast<double>(qn));
             const double eps = METRIC == 0 ? p.gamma * (sq + R) * (sq + R) : p.gamma * sq * R;
@@ -214,9 +221,9 @@ __global__ void __launch_bounds__(32 * kRerankWarps) rerank_kernel(const RerankP
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) kth = max(kth, __shfl_xor_sync(0xffffffffu, kth, o));
-        if (lane == 0 && p.c < p.n - 1) {
+        if (lane == 0 && p.c < eligible) {
             // Proof that the excluded rows cannot enter the top k.
-            const float qn = p.norms[q];
+            const float qn = p.q_norms[qi];
             const double R = static_cast<double>(__uint_as_float(*p.max_norm_bits));
             const double a_c = static_cast<double>(key_to_float(p.cand_keys[qi * p.c + p.c - 1]));
             double approx_bound, eps;

@@ -16,6 +16,7 @@
 #include <string>
 
 #include "knn_exact.cuh"
+#include "knn_pair.cuh"
 #include "knn_rerank.cuh"
 #include "knn_tc.cuh"
 #include "knng_gpu.h"
@@ -47,6 +48,26 @@ knng_gpu_status fail(knng_gpu_status s, const std::string& msg)
     } while (0)
 
 constexpr uint64_t align_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
+
+#ifdef KNNG_GPU_EXPERIMENTS
+constexpr bool kExperiments = true;
+#else
+constexpr bool kExperiments = false;
+#endif
+
+// Tuning knobs for kernel experiments (grid size, stages, tile shape,
+// profiling modes). Only a build compiled with -DKNNG_GPU_EXPERIMENTS reads
+// them; the shipped library never looks at the environment, so no variable
+// can change what a build computes.
+const char* experiment_knob(const char* name)
+{
+#ifdef KNNG_GPU_EXPERIMENTS
+    return std::getenv(name);
+#else
+    (void)name;
+    return nullptr;
+#endif
+}
 
 // Argument checks and messages of brute_force.hpp:339-352.
 knng_gpu_status validate(uint64_t n, uint64_t d, uint64_t k, int metric)
@@ -226,6 +247,23 @@ knng_gpu_status make_map(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t e
     return KNNG_GPU_OK;
 }
 
+// 1-D map over n int32 values, boxes of `box` elements (zero fill past n).
+knng_gpu_status make_map_1d_i32(CUtensorMap* map, const void* base, uint64_t n, uint32_t box)
+{
+    EncodeTiledFn enc;
+    KNNG_TRY(get_encode_fn(&enc));
+    const cuuint64_t dims[1] = {n};
+    const cuuint64_t strides[1] = {4};
+    const cuuint32_t boxd[1] = {box};
+    const cuuint32_t estr[1] = {1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_INT32, 1, const_cast<void*>(base), dims, strides, boxd, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(KNNG_GPU_CUDA_ERROR, "knng::gpu: cuTensorMapEncodeTiled (1-D) failed (" + std::to_string(int(r)) + ")");
+    return KNNG_GPU_OK;
+}
+
 // Packed u8 row: the data (d rounded up to 128 bytes), then kAugBytes of
 // augmentation.
 uint64_t u8_data_bytes(uint64_t d) { return align_up(d == 0 ? 1 : d, kChunkBytes); }
@@ -239,23 +277,42 @@ int sm_count()
 }
 
 // ------------------------------------------------------------------ launch helpers
+// Scratch of a u8 search: the fallback-row list (one entry per query), two
+// counters (fallback count, error word), then the partial (key, id) lists of
+// query tiles that the pair kernel cuts between CTA pairs (two lists of 256
+// rows x k per pair). Without the partial region the single-CTA kernel runs.
 struct ScratchU8 {
     uint32_t* fallback_rows;
     uint32_t* counters;  // [0] fallback count, [1] error flag
+    int32_t* part_keys;
+    uint32_t* part_ids;
+    uint32_t part_pairs;  // CTA pairs whose partial lists fit
 };
 
-// Concurrent base ranges for the last partial wave of query tiles.
-constexpr int kMaxTailParts = 8;
+// CTA pairs a device can hold at once (one pair per two SMs).
+uint32_t max_pairs() { return static_cast<uint32_t>(std::max(1, sm_count() / 2)); }
 
-// Fallback-row list (one entry per query) + 2 counters per launch (at most
-// kMaxTailParts + 1 launches: 72 bytes of the 256).
-uint64_t scratch_u8_bytes(uint64_t q_count) { return align_up(q_count * 4, 256) + 256; }
+uint64_t partial_bytes_per_pair(uint64_t k) { return 2ull * kPairTile * k * 8; }
 
-ScratchU8 carve_scratch_u8(void* p, uint64_t q_count)
+uint64_t scratch_u8_base_bytes(uint64_t q_count) { return align_up(q_count * 4, 256) + 256; }
+
+uint64_t scratch_u8_bytes(uint64_t q_count, uint64_t k)
 {
-    ScratchU8 s;
-    s.fallback_rows = static_cast<uint32_t*>(p);
-    s.counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(p) + align_up(q_count * 4, 256));
+    return scratch_u8_base_bytes(q_count) + align_up(max_pairs() * partial_bytes_per_pair(k), 256);
+}
+
+ScratchU8 carve_scratch_u8(void* p, uint64_t q_count, uint64_t k, uint64_t bytes)
+{
+    ScratchU8 s{};
+    uint8_t* b = static_cast<uint8_t*>(p);
+    s.fallback_rows = reinterpret_cast<uint32_t*>(b);
+    s.counters = reinterpret_cast<uint32_t*>(b + align_up(q_count * 4, 256));
+    const uint64_t base = scratch_u8_base_bytes(q_count);
+    const uint64_t rest = bytes > base ? bytes - base : 0;
+    const uint64_t per_pair = partial_bytes_per_pair(k);
+    s.part_pairs = static_cast<uint32_t>(std::min<uint64_t>(rest / per_pair, 1u << 16));
+    s.part_keys = reinterpret_cast<int32_t*>(b + base);
+    s.part_ids = reinterpret_cast<uint32_t*>(b + base + s.part_pairs * per_pair / 2);
     return s;
 }
 
@@ -273,7 +330,7 @@ knng_gpu_status launch_tc_t(const TcMaps& m, const KnnTcParams& p, cudaStream_t 
     KNNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const uint32_t n_qtiles = (p.n_queries + MT * kTileRows - 1) / (MT * kTileRows);
     uint32_t grid = std::min<uint32_t>(n_qtiles, static_cast<uint32_t>(sm_count()));
-    if (const char* gv = std::getenv("KNNG_GPU_GRID")) grid = std::min<uint32_t>(grid, std::max(1, std::atoi(gv)));  // experiments only
+    if (const char* gv = experiment_knob("KNNG_GPU_GRID")) grid = std::min<uint32_t>(grid, std::max(1, std::atoi(gv)));  // experiments only
     kern<<<grid, 64 + 128 * MT * SPLIT, smem, st>>>(m.q0, m.q1, m.b0, m.b1, p);
     KNNG_CUDA(cudaGetLastError());
     return KNNG_GPU_OK;
@@ -287,7 +344,7 @@ uint32_t pick_stages(int planes, int mt, bool a_stream, uint32_t kchunks, int sp
     const uint32_t budget = 227u * 1024u - 1024u;
     if (L0.total >= budget) return 0;
     uint32_t s = std::min<uint32_t>(16, (budget - L0.total) / L0.stage_bytes);
-    if (const char* sv = std::getenv("KNNG_GPU_STAGES")) s = std::min<uint32_t>(s, std::atoi(sv));
+    if (const char* sv = experiment_knob("KNNG_GPU_STAGES")) s = std::min<uint32_t>(s, std::atoi(sv));
     return s;
 }
 
@@ -346,22 +403,33 @@ knng_gpu_status launch_exact(const KnnExactParams<T>& p, int metric, uint32_t ma
 // the exact kernel on the packed bytes.
 constexpr uint64_t kMaxTensorDim = 1024;
 
-// Device interval timer; ms() is 0 unless both ends were recorded (an
-// elapsed-time query on an unrecorded event would leave a sticky error).
+constexpr int kMaxDevices = 64;
+
+// Timing events, created once per (host thread, device) and reused by every
+// later call, so a call that fills stats creates no CUDA objects after the
+// first one on its thread.
+cudaEvent_t timing_event(int slot)
+{
+    thread_local cudaEvent_t ev[kMaxDevices][10] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || slot < 0 || slot >= 10) return nullptr;
+    if (!ev[dev][slot] && cudaEventCreate(&ev[dev][slot]) != cudaSuccess) ev[dev][slot] = nullptr;
+    return ev[dev][slot];
+}
+
+// Device interval timer on the cached events of timer index `id` (0..4);
+// ms() is 0 unless both ends were recorded (an elapsed-time query on an
+// unrecorded event would leave a sticky error).
 struct EventTimer {
     cudaEvent_t a = nullptr, b = nullptr;
     bool on, started = false, stopped = false;
-    explicit EventTimer(bool enable) : on(enable)
+    EventTimer(bool enable, int id) : on(enable)
     {
         if (on) {
-            cudaEventCreate(&a);
-            cudaEventCreate(&b);
+            a = timing_event(2 * id);
+            b = timing_event(2 * id + 1);
+            on = a && b;
         }
-    }
-    ~EventTimer()
-    {
-        if (a) cudaEventDestroy(a);
-        if (b) cudaEventDestroy(b);
     }
     void start(cudaStream_t s)
     {
@@ -411,7 +479,7 @@ struct U8Sets {
 int u8_query_tiles_per_cta(uint64_t d, uint64_t k)
 {
     int mt = (u8_data_bytes(d) / kChunkBytes <= 2 && k <= 32) ? 2 : 1;
-    if (const char* mv = std::getenv("KNNG_GPU_MT")) mt = std::atoi(mv) == 1 ? 1 : mt;  // experiments only
+    if (const char* mv = experiment_knob("KNNG_GPU_MT")) mt = std::atoi(mv) == 1 ? 1 : mt;  // experiments only
     return mt;
 }
 
@@ -470,14 +538,14 @@ knng_gpu_status launch_u8_sets(const U8Sets& z, uint64_t d, uint64_t k, int metr
         p.fallback_rows = sc.fallback_rows;
         p.fallback_count = sc.counters;
         p.error = reinterpret_cast<int*>(sc.counters + 1);
-        if (const char* dbg = std::getenv("KNNG_GPU_DEBUG_FLAGS")) p.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
+        if (const char* dbg = experiment_knob("KNNG_GPU_DEBUG_FLAGS")) p.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
         int mt = u8_query_tiles_per_cta(d, k);
         // Optional column-split epilogue (four epilogue warps per SM
         // sub-partition, each on half of a 256-column tile), KNNG_GPU_SPLIT=2.
         // Measured slower than one warp per 32 rows at n=1M d=128 k=10 on B200
         // (305 ms vs 263 ms: the 96-register budget spills), so off by default.
         int split = 1;
-        if (const char* sv = std::getenv("KNNG_GPU_SPLIT")) split = (std::atoi(sv) == 2 && mt == 2 && k <= 16) ? 2 : 1;
+        if (const char* sv = experiment_knob("KNNG_GPU_SPLIT")) split = (std::atoi(sv) == 2 && mt == 2 && k <= 16) ? 2 : 1;
         const bool aug = metric == 0;
         p.stages = pick_stages(1, mt, false, p.kchunks, split, split > 1 ? (k <= 10 ? 10 : 16) : 0, aug);
         if (split > 1 && p.stages < 3) {
@@ -487,7 +555,7 @@ knng_gpu_status launch_u8_sets(const U8Sets& z, uint64_t d, uint64_t k, int metr
         if (p.stages < 2 || (mt > 1 && p.stages < p.kchunks))
             return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: shared memory budget exceeded");
         unsigned long long* dbg_clk = nullptr;
-        if (p.debug_flags & 512u) {  // profiling only
+        if (kExperiments && (p.debug_flags & 512u)) {  // profiling only
             cudaMalloc(&dbg_clk, 8 * sizeof(unsigned long long));
             cudaMemsetAsync(dbg_clk, 0, 8 * sizeof(unsigned long long), st);
             p.debug_clocks = dbg_clk;
@@ -523,137 +591,190 @@ knng_gpu_status launch_u8_sets(const U8Sets& z, uint64_t d, uint64_t k, int metr
     return KNNG_GPU_OK;
 }
 
-__global__ void merge_topk_kernel(const uint32_t* __restrict__ a_ids, const float* __restrict__ a_d,
-                                  const uint32_t* __restrict__ b_ids, const float* __restrict__ b_d, uint64_t rows,
-                                  uint32_t k, uint32_t* __restrict__ o_ids, float* __restrict__ o_d);
-
-// Streams and events of one split search, released on every exit path.
-struct ForkSet {
-    cudaStream_t s[kMaxTailParts] = {};
-    cudaEvent_t fork = nullptr, join[kMaxTailParts] = {};
-    ~ForkSet()
-    {
-        for (int i = 0; i < kMaxTailParts; ++i) {
-            if (join[i]) cudaEventDestroy(join[i]);
-            if (s[i]) cudaStreamDestroy(s[i]);
-        }
-        if (fork) cudaEventDestroy(fork);
-    }
+// Options of one u8 search that only internal callers set.
+struct U8RunOptions {
+    bool allow_pair = true;                  // CTA-pair kernel where it applies
+    long long wait_limit = kSpinLimitCycles;  // bound of every device-side wait
+    uint32_t test_mode = 0;                  // 1: the pair kernel withholds one arrival
+    bool timing = true;                      // fill the *_ms fields of stats
+    const int* skip_flag = nullptr;          // pair kernel: device flag, non-zero = data not integer-valued
 };
 
-// u8 search of a query set against a base set. The fused kernel is
-// persistent with one CTA per SM over query tiles; when the last wave would
-// hold only R < SMs/2 tiles, those tail queries are searched first by
-// f = SMs / R concurrent launches, each over one 256-row-aligned range of the
-// base, and the f exact partial lists are merged by (distance, id). Their
-// temporary rows live in the output rows of the main range, which the main
-// launch then overwrites. The result is identical to one pass.
+struct PairMaps {
+    CUtensorMap q, b, baug, norm;
+};
+
+template <int METRIC, int KC>
+knng_gpu_status launch_pair_t(const PairMaps& m, PairParams& pp, uint32_t max_pairs_fit, cudaStream_t st,
+                              uint32_t* launches, EventTimer* tt)
+{
+    const SmemLayoutPair L = smem_layout_pair(pp.kchunks, pp.stages, METRIC == 0);
+    const uint32_t smem = L.total + 1024;
+    auto kern = knn_pair_kernel<METRIC, RegTopK<KC>>;
+    KNNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kPairThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(2 * max_pairs());
+    int clusters = 0;
+    KNNG_CUDA(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+    uint64_t np = std::min<uint64_t>(static_cast<uint64_t>(std::max(clusters, 0)), max_pairs_fit);
+    np = std::min<uint64_t>(np, pp.total);
+    if (const char* gv = experiment_knob("KNNG_GPU_PAIRS")) np = std::min<uint64_t>(np, std::max(1, std::atoi(gv)));
+    if (np == 0) return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: no CTA pair fits on this device");
+    pp.n_pairs = static_cast<uint32_t>(np);
+    cfg.gridDim = dim3(2 * pp.n_pairs);
+    if (tt) tt->start(st);
+    KNNG_CUDA(cudaLaunchKernelEx(&cfg, kern, m.q, m.b, m.baug, m.norm, pp));
+    if (tt) tt->stop(st);
+    ++*launches;
+    if (pp.n_pairs > 1) {
+        merge_pair_partials<METRIC, KC><<<pp.n_pairs - 1, kPairTile, 0, st>>>(pp);
+        KNNG_CUDA(cudaGetLastError());
+        ++*launches;
+    }
+    return KNNG_GPU_OK;
+}
+
+template <int METRIC>
+knng_gpu_status launch_pair_k(const PairMaps& m, PairParams& pp, uint32_t fit, cudaStream_t st, uint32_t* launches,
+                              EventTimer* tt)
+{
+    if (pp.k <= 10) return launch_pair_t<METRIC, 10>(m, pp, fit, st, launches, tt);
+    if (pp.k <= 16) return launch_pair_t<METRIC, 16>(m, pp, fit, st, launches, tt);
+    if (pp.k <= 32) return launch_pair_t<METRIC, 32>(m, pp, fit, st, launches, tt);
+    return launch_pair_t<METRIC, 64>(m, pp, fit, st, launches, tt);
+}
+
+// Stages of the pair kernel that fit the shared-memory budget (0: none).
+uint32_t pick_pair_stages(uint32_t kchunks, bool l2)
+{
+    const SmemLayoutPair L0 = smem_layout_pair(kchunks, 0, l2);
+    const uint32_t budget = 227u * 1024u - 1024u;
+    if (L0.total >= budget) return 0;
+    uint32_t s = std::min<uint32_t>(16, (budget - L0.total) / L0.stage_bytes);
+    if (const char* sv = experiment_knob("KNNG_GPU_STAGES")) s = std::min<uint32_t>(s, std::atoi(sv));
+    return s >= 2 ? s : 0;
+}
+
+// The pair kernel: base and query rows in 256-row tiles on CTA pairs,
+// stream-K split, then the exact kernel on the rows it flags.
+knng_gpu_status launch_u8_pair(const U8Sets& z, uint64_t d, uint64_t k, int metric, uint32_t* ids, float* dists,
+                               const ScratchU8& sc, const U8RunOptions& opt, cudaStream_t st, uint32_t* launches,
+                               EventTimer* tt)
+{
+    const uint64_t pitch = knng_gpu_padded_dim(d);
+    const uint64_t data_bytes = u8_data_bytes(d);
+    PairMaps m;
+    KNNG_TRY(make_map(&m.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.q_packed, z.n_q, data_bytes, pitch));
+    KNNG_TRY(make_map(&m.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.b_packed, z.n_b, data_bytes, pitch));
+    if (metric == 0) {
+        KNNG_TRY(make_map(&m.baug, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.b_packed + data_bytes, z.n_b, kAugBytes, pitch,
+                          kAugBytes));
+        KNNG_TRY(make_map_1d_i32(&m.norm, z.b_norms, z.n_b, kPairTile));
+    } else {
+        m.baug = m.b;
+        m.norm = m.b;
+    }
+    PairParams pp{};
+    pp.query_norms = z.q_norms;
+    pp.query_packed = z.q_packed;
+    pp.pitch = static_cast<uint32_t>(pitch);
+    pp.data_bytes = static_cast<uint32_t>(data_bytes);
+    pp.n_base = z.n_b;
+    pp.base_id0 = static_cast<uint32_t>(z.b_id0);
+    pp.n_queries = static_cast<uint32_t>(z.n_q);
+    pp.query_id0 = static_cast<uint32_t>(z.q_id0);
+    pp.exclude_self = z.exclude_self;
+    pp.k = static_cast<uint32_t>(k);
+    pp.kchunks = static_cast<uint32_t>(data_bytes / kChunkBytes);
+    pp.stages = pick_pair_stages(pp.kchunks, metric == 0);
+    pp.n_qtiles = static_cast<uint32_t>((z.n_q + kPairTile - 1) / kPairTile);
+    pp.n_btiles = static_cast<uint32_t>((z.n_b + kPairTile - 1) / kPairTile);
+    pp.total = static_cast<uint64_t>(pp.n_qtiles) * pp.n_btiles;
+    pp.out_ids = ids;
+    pp.out_dists = dists;
+    pp.part_keys = sc.part_keys;
+    pp.part_ids = sc.part_ids;
+    pp.fallback_rows = sc.fallback_rows;
+    pp.fallback_count = sc.counters;
+    pp.error = reinterpret_cast<int*>(sc.counters + 1);
+    pp.wait_limit = opt.wait_limit;
+    pp.test_mode = opt.test_mode;
+    pp.skip_flag = opt.skip_flag;
+    if (const char* dbg = experiment_knob("KNNG_GPU_DEBUG_FLAGS")) pp.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
+    KNNG_TRY(metric == 0 ? launch_pair_k<0>(m, pp, sc.part_pairs, st, launches, tt)
+                         : launch_pair_k<1>(m, pp, sc.part_pairs, st, launches, tt));
+    // Rows whose fp32 sums may round: recompute exactly (device-side count).
+    KnnExactParams<uint8_t> e{};
+    e.base = z.b_packed;
+    e.base_stride = pitch;
+    e.n_base = z.n_b;
+    e.base_id0 = static_cast<uint32_t>(z.b_id0);
+    e.queries = z.q_packed;
+    e.query_stride = pitch;
+    e.n_queries = static_cast<uint32_t>(z.n_q);
+    e.query_id0 = static_cast<uint32_t>(z.q_id0);
+    e.exclude_self = z.exclude_self;
+    e.d = static_cast<uint32_t>(d);
+    e.k = static_cast<uint32_t>(k);
+    e.out_ids = ids;
+    e.out_dists = dists;
+    e.row_list = sc.fallback_rows;
+    e.row_count = sc.counters;
+    KNNG_TRY(launch_exact(e, metric, static_cast<uint32_t>(z.n_q), st));
+    ++*launches;
+    return KNNG_GPU_OK;
+}
+
+// Whether the pair kernel applies: d <= 1024 with a stage budget, k <= 64
+// (register lists), partial-list scratch present, and 16-byte aligned key
+// offsets (TMA source).
+bool pair_applies(const U8Sets& z, uint64_t d, uint64_t k, int metric, const ScratchU8& sc, const U8RunOptions& opt)
+{
+    if (!opt.allow_pair || d > kMaxTensorDim || k > 64 || sc.part_pairs == 0) return false;
+    if (const char* pv = experiment_knob("KNNG_GPU_PAIR")) if (std::atoi(pv) == 0) return false;
+    if (metric == 0 && (reinterpret_cast<uintptr_t>(z.b_norms) & 15)) return false;
+    return pick_pair_stages(static_cast<uint32_t>(u8_data_bytes(d) / kChunkBytes), metric == 0) >= 2;
+}
+
+// u8 search of a query set against a base set: the pair kernel where it
+// applies, else the single-CTA kernel; then the exact kernel for flagged rows.
+// One host synchronisation at the end reads the fallback count and the error
+// word.
 knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int metric, uint32_t* ids, float* dists,
                                  void* scratch, uint64_t scratch_bytes, cudaStream_t st, knng_gpu_stats* stats,
-                                 bool allow_split = true)
+                                 const U8RunOptions& opt = U8RunOptions())
 {
     const uint64_t q_count = z.n_q;
-    if (scratch_bytes < scratch_u8_bytes(q_count))
+    if (scratch_bytes < scratch_u8_base_bytes(q_count))
         return fail(KNNG_GPU_WORKSPACE_TOO_SMALL, "knng::gpu: scratch smaller than knng_gpu_knn_scratch_bytes");
     if (q_count == 0) return KNNG_GPU_OK;
     if (z.n_b < k + (z.exclude_self ? 1 : 0))
         return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: fewer base rows than k");
-    const uint64_t pitch = knng_gpu_padded_dim(d);
-    const ScratchU8 sc = carve_scratch_u8(scratch, q_count);
-    // Tail plan.
-    const uint64_t sms = static_cast<uint64_t>(sm_count());
-    const uint64_t qt_rows = static_cast<uint64_t>(u8_query_tiles_per_cta(d, k)) * kTileRows;
-    const uint64_t qtiles = (q_count + qt_rows - 1) / qt_rows;
-    const uint64_t full_waves = qtiles / sms, tail_tiles = qtiles % sms;
-    uint64_t parts = tail_tiles ? std::min<uint64_t>(kMaxTailParts, sms / tail_tiles) : 0;
-    uint64_t part_rows = 0;
-    if (parts >= 2) {
-        part_rows = align_up((z.n_b + parts - 1) / parts, 256);
-        parts = (z.n_b + part_rows - 1) / part_rows;
-        // every part needs k (+ self) rows
-        if (part_rows < k + 1 || z.n_b - (parts - 1) * part_rows < k + 1) parts = 0;
-    }
-    bool split = allow_split && d <= kMaxTensorDim && full_waves >= 1 && parts >= 2;
-    if (const char* tv = std::getenv("KNNG_GPU_TAIL_SPLIT")) split = split && std::atoi(tv) != 0;  // experiments
-    const uint64_t main_q = split ? full_waves * sms * qt_rows : q_count;
-    const uint64_t tail_q = q_count - main_q;
-    const uint32_t n_launch = split ? static_cast<uint32_t>(parts) + 1 : 1;
-    KNNG_CUDA(cudaMemsetAsync(sc.counters, 0, 8 * n_launch, st));
+    const ScratchU8 sc = carve_scratch_u8(scratch, q_count, k, scratch_bytes);
+    KNNG_CUDA(cudaMemsetAsync(sc.counters, 0, 8, st));
     uint32_t launches = 0;
-    EventTimer tk(stats != nullptr), tf(stats != nullptr && !split);
+    const bool timing = stats != nullptr && opt.timing;
+    EventTimer tk(timing, 2), tf(timing, 3), tt(timing, 4);
     tk.start(st);
-    if (split) {
-        ForkSet fs;
-        KNNG_CUDA(cudaEventCreateWithFlags(&fs.fork, cudaEventDisableTiming));
-        KNNG_CUDA(cudaEventRecord(fs.fork, st));
-        for (uint64_t pi = 0; pi < parts; ++pi) {
-            KNNG_CUDA(cudaStreamCreateWithFlags(&fs.s[pi], cudaStreamNonBlocking));
-            KNNG_CUDA(cudaEventCreateWithFlags(&fs.join[pi], cudaEventDisableTiming));
-            KNNG_CUDA(cudaStreamWaitEvent(fs.s[pi], fs.fork, 0));
-            const uint64_t b0 = pi * part_rows;
-            U8Sets zp = z;
-            zp.q_packed = z.q_packed + main_q * pitch;
-            zp.q_norms = z.q_norms + main_q;
-            zp.n_q = tail_q;
-            zp.q_id0 = z.q_id0 + main_q;
-            zp.b_packed = z.b_packed + b0 * pitch;
-            zp.b_norms = z.b_norms + b0;
-            zp.n_b = std::min(part_rows, z.n_b - b0);
-            zp.b_id0 = z.b_id0 + b0;
-            const ScratchU8 scp{sc.fallback_rows + pi * tail_q, sc.counters + 2 * (1 + pi)};
-            KNNG_TRY(launch_u8_sets(zp, d, k, metric, ids + pi * tail_q * k, dists + pi * tail_q * k, scp, fs.s[pi],
-                                    &launches, nullptr));
-            KNNG_CUDA(cudaEventRecord(fs.join[pi], fs.s[pi]));
-            KNNG_CUDA(cudaStreamWaitEvent(st, fs.join[pi], 0));
-        }
-        // Fold the partial lists into the tail rows, alternating between the
-        // tail rows and part 0's temporary rows (free after the first merge)
-        // so that no merge writes the list it reads.
-        uint32_t* t_ids = ids + main_q * k;
-        float* t_d = dists + main_q * k;
-        const uint32_t blocks = static_cast<uint32_t>((tail_q + 255) / 256);
-        bool in_tail = false;  // the running result: part 0's rows at first
-        for (uint64_t pi = 1; pi < parts; ++pi) {
-            const uint32_t* a_ids = in_tail ? t_ids : ids;
-            const float* a_d = in_tail ? t_d : dists;
-            uint32_t* o_ids = in_tail ? ids : t_ids;
-            float* o_d = in_tail ? dists : t_d;
-            merge_topk_kernel<<<blocks, 256, 0, st>>>(a_ids, a_d, ids + pi * tail_q * k, dists + pi * tail_q * k,
-                                                      tail_q, static_cast<uint32_t>(k), o_ids, o_d);
-            KNNG_CUDA(cudaGetLastError());
-            ++launches;
-            in_tail = !in_tail;
-        }
-        if (!in_tail) {
-            KNNG_CUDA(cudaMemcpyAsync(t_ids, ids, tail_q * k * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
-            KNNG_CUDA(cudaMemcpyAsync(t_d, dists, tail_q * k * sizeof(float), cudaMemcpyDeviceToDevice, st));
-        }
-        U8Sets zm = z;
-        zm.n_q = main_q;
-        KNNG_TRY(launch_u8_sets(zm, d, k, metric, ids, dists, ScratchU8{sc.fallback_rows, sc.counters}, st,
-                                &launches, nullptr));
+    if (pair_applies(z, d, k, metric, sc, opt)) {
+        KNNG_TRY(launch_u8_pair(z, d, k, metric, ids, dists, sc, opt, st, &launches, &tt));
         tk.stop(st);
-        uint32_t host_counters[2 * (kMaxTailParts + 1)] = {};
-        KNNG_CUDA(cudaMemcpyAsync(host_counters, sc.counters, 8 * n_launch, cudaMemcpyDeviceToHost, st));
-        KNNG_CUDA(cudaStreamSynchronize(st));
-        uint32_t fallback = 0;
-        for (uint32_t i = 0; i < n_launch; ++i) {
-            if (host_counters[2 * i + 1] != 0)
-                return fail(KNNG_GPU_TIMEOUT, "knng::gpu: a bounded device wait gave up (code " +
-                                                  std::to_string(host_counters[2 * i + 1]) + ")");
-            fallback += host_counters[2 * i];
-        }
-        if (stats) {
-            stats->path = KNNG_PATH_U8_TENSOR;
-            stats->fallback_rows = fallback;
-            stats->knn_ms = tk.ms();
-            stats->fallback_ms = 0.f;
-            stats->kernel_launches += launches;
-        }
-        return KNNG_GPU_OK;
+    } else {
+        tt.start(st);
+        KNNG_TRY(launch_u8_sets(z, d, k, metric, ids, dists, sc, st, &launches, &tf));
+        tt.stop(st);
+        tk.stop(st);
     }
-    KNNG_TRY(launch_u8_sets(z, d, k, metric, ids, dists, sc, st, &launches, &tf));
-    tk.stop(st);
     uint32_t host_counters[2] = {0, 0};
     KNNG_TRY(read_counters(sc.counters, host_counters, st));
     if (stats) {
@@ -661,6 +782,7 @@ knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int me
         stats->fallback_rows = host_counters[0];
         stats->knn_ms = tk.ms();
         stats->fallback_ms = tf.ms();
+        stats->tc_ms = tt.ms();
         stats->kernel_launches += launches;
     }
     return KNNG_GPU_OK;
@@ -668,12 +790,13 @@ knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int me
 
 knng_gpu_status knn_u8_impl(const uint8_t* packed, const int32_t* norms, uint64_t n, uint64_t d, uint64_t q_begin,
                             uint64_t q_count, uint64_t k, int metric, uint32_t* ids, float* dists, void* scratch,
-                            uint64_t scratch_bytes, cudaStream_t st, knng_gpu_stats* stats, bool allow_split = true)
+                            uint64_t scratch_bytes, cudaStream_t st, knng_gpu_stats* stats,
+                            const U8RunOptions& opt = U8RunOptions())
 {
     if (q_begin + q_count > n) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: query range exceeds the base");
     const uint64_t pitch = knng_gpu_padded_dim(d);
     const U8Sets z{packed + q_begin * pitch, norms + q_begin, q_count, q_begin, packed, norms, n, 0, 1};
-    return knn_u8_sets_impl(z, d, k, metric, ids, dists, scratch, scratch_bytes, st, stats, allow_split);
+    return knn_u8_sets_impl(z, d, k, metric, ids, dists, scratch, scratch_bytes, st, stats, opt);
 }
 
 // Merge two row-wise sorted k-lists into the k best by (distance, id) -- the
@@ -709,8 +832,12 @@ __global__ void merge_topk_kernel(const uint32_t* __restrict__ a_ids, const floa
 }
 
 // ------------------------------------------------------------------ fp32 path
-// Candidates kept per row by the bf16x3 filter: k plus a margin, at most n - 1.
-uint64_t f32_candidates(uint64_t n, uint64_t k) { return std::min<uint64_t>(n - 1, k + 32); }
+// Candidates kept per query row by the bf16x3 filter: k plus a margin, at
+// most the rows a query can see (n_b, minus itself when excluded).
+uint64_t f32_candidates_sets(uint64_t n_b, int exclude_self, uint64_t k)
+{
+    return std::min<uint64_t>(n_b - (exclude_self ? 1 : 0), k + 32);
+}
 
 uint64_t f32_pitch_elems(uint64_t d) { return align_up(d, kChunkBytes / 2); }
 
@@ -718,9 +845,12 @@ struct ScratchF32 {
     double* sums;
     float* mu;
     unsigned int* max_norm_bits;
-    __nv_bfloat16* hi;
+    __nv_bfloat16* hi;  // base planes
     __nv_bfloat16* lo;
     float* norms;
+    __nv_bfloat16* q_hi;  // query planes (separate query set only)
+    __nv_bfloat16* q_lo;
+    float* q_norms;
     uint32_t* cand_ids;
     int32_t* cand_keys;
     uint32_t* fallback_rows;
@@ -728,7 +858,8 @@ struct ScratchF32 {
     uint64_t total;
 };
 
-ScratchF32 layout_scratch_f32(void* base, uint64_t n, uint64_t d, uint64_t q_count, uint64_t k)
+ScratchF32 layout_scratch_f32_sets(void* base, uint64_t n_b, uint64_t n_q, uint64_t d, uint64_t k, int exclude_self,
+                                   bool separate_q)
 {
     ScratchF32 s{};
     uint8_t* p = static_cast<uint8_t*>(base);
@@ -739,19 +870,30 @@ ScratchF32 layout_scratch_f32(void* base, uint64_t n, uint64_t d, uint64_t q_cou
         return r;
     };
     const uint64_t pitch = f32_pitch_elems(d);
-    const uint64_t c = f32_candidates(n, k);
+    const uint64_t c = f32_candidates_sets(n_b, exclude_self, k);
     s.sums = reinterpret_cast<double*>(take(d * 8));
     s.mu = reinterpret_cast<float*>(take(d * 4));
     s.max_norm_bits = reinterpret_cast<unsigned int*>(take(4));
-    s.hi = reinterpret_cast<__nv_bfloat16*>(take(n * pitch * 2));
-    s.lo = reinterpret_cast<__nv_bfloat16*>(take(n * pitch * 2));
-    s.norms = reinterpret_cast<float*>(take(n * 4));
-    s.cand_ids = reinterpret_cast<uint32_t*>(take(q_count * c * 4));
-    s.cand_keys = reinterpret_cast<int32_t*>(take(q_count * c * 4));
-    s.fallback_rows = reinterpret_cast<uint32_t*>(take(q_count * 4));
+    s.hi = reinterpret_cast<__nv_bfloat16*>(take(n_b * pitch * 2));
+    s.lo = reinterpret_cast<__nv_bfloat16*>(take(n_b * pitch * 2));
+    s.norms = reinterpret_cast<float*>(take(n_b * 4));
+    if (separate_q) {
+        s.q_hi = reinterpret_cast<__nv_bfloat16*>(take(n_q * pitch * 2));
+        s.q_lo = reinterpret_cast<__nv_bfloat16*>(take(n_q * pitch * 2));
+        s.q_norms = reinterpret_cast<float*>(take(n_q * 4));
+    }
+    s.cand_ids = reinterpret_cast<uint32_t*>(take(n_q * c * 4));
+    s.cand_keys = reinterpret_cast<int32_t*>(take(n_q * c * 4));
+    s.fallback_rows = reinterpret_cast<uint32_t*>(take(n_q * 4));
     s.counters = reinterpret_cast<uint32_t*>(take(16));
     s.total = off;
     return s;
+}
+
+// Self graph: queries are rows of the base (planes shared).
+ScratchF32 layout_scratch_f32(void* base, uint64_t n, uint64_t d, uint64_t q_count, uint64_t k)
+{
+    return layout_scratch_f32_sets(base, n, q_count, d, k, 1, false);
 }
 
 // eps coefficient of the re-rank proof (knn_rerank.cuh).
@@ -760,65 +902,92 @@ double f32_gamma(uint64_t d, int metric)
     const double dd = static_cast<double>(d);
     const double split = std::ldexp(1.0, -14), acc = (3.0 * dd / 16.0 + 3.0) * std::ldexp(1.0, -22);
     const double ref = (dd + 3.0) * std::ldexp(1.0, -24);
-    double g = metric == 0 ? 2.0 * (split + acc) + std::ldexp(1.0, -19) + ref : split + acc + std::ldexp(1.0, -21) + ref;
-    if (const char* gs = std::getenv("KNNG_GPU_GAMMA_SCALE")) g *= std::atof(gs);  // experiments only
-    return g;
+    return metric == 0 ? 2.0 * (split + acc) + std::ldexp(1.0, -19) + ref : split + acc + std::ldexp(1.0, -21) + ref;
 }
 
-knng_gpu_status knn_f32_impl(const float* x, uint64_t n, uint64_t d, uint64_t q_begin, uint64_t q_count, uint64_t k,
-                             int metric, uint32_t* ids, float* dists, void* scratch, uint64_t scratch_bytes,
-                             cudaStream_t st, knng_gpu_stats* stats)
+// fp32 query rows against fp32 base rows. Ids are global (base row r is
+// b_id0 + r, query i is q_id0 + i); with exclude_self a query never returns
+// its own id. q_row_in_b >= 0: the queries are rows [q_row_in_b, +n_q) of the
+// base itself, whose hi/lo planes then serve both sides.
+struct F32Sets {
+    const float* q;
+    uint64_t n_q, q_id0;
+    const float* b;
+    uint64_t n_b, b_id0;
+    int exclude_self;
+    int64_t q_row_in_b;
+};
+
+knng_gpu_status knn_f32_sets_impl(const F32Sets& z, uint64_t d, uint64_t k, int metric, uint32_t* ids, float* dists,
+                                  void* scratch, uint64_t scratch_bytes, cudaStream_t st, knng_gpu_stats* stats)
 {
-    if (q_begin + q_count > n) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: query range exceeds the base");
-    const ScratchF32 sc = layout_scratch_f32(scratch, n, d, q_count, k);
+    const bool separate = z.q_row_in_b < 0;
+    const ScratchF32 sc = layout_scratch_f32_sets(scratch, z.n_b, z.n_q, d, k, z.exclude_self, separate);
     if (scratch_bytes < sc.total || (reinterpret_cast<uintptr_t>(scratch) & 255))
         return fail(KNNG_GPU_WORKSPACE_TOO_SMALL, "knng::gpu: fp32 scratch smaller than knng_gpu_knn_f32_scratch_bytes");
-    if (q_count == 0) return KNNG_GPU_OK;
+    if (z.n_q == 0) return KNNG_GPU_OK;
+    if (z.n_b < k + (z.exclude_self ? 1 : 0)) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: fewer base rows than k");
     const uint64_t pitch = f32_pitch_elems(d);
-    const uint64_t c = f32_candidates(n, k);
+    const uint64_t c = f32_candidates_sets(z.n_b, z.exclude_self, k);
     const uint32_t kchunks = static_cast<uint32_t>(pitch * 2 / kChunkBytes);
-    EventTimer tk(stats != nullptr), tf(stats != nullptr);
+    EventTimer tk(stats != nullptr, 2), tf(stats != nullptr, 3);
     tk.start(st);
     KNNG_CUDA(cudaMemsetAsync(sc.counters, 0, 16, st));
     KNNG_CUDA(cudaMemsetAsync(sc.max_norm_bits, 0, 4, st));
     uint32_t launches = 0;
     if (metric == 0) {
-        // L2 is translation invariant: centre the rows to shrink the error bound.
+        // L2 is translation invariant: centre both sets on the base's mean to
+        // shrink the error bound.
         KNNG_CUDA(cudaMemsetAsync(sc.sums, 0, d * 8, st));
-        column_sum_kernel<<<static_cast<uint32_t>((n + 255) / 256), 256, 0, st>>>(x, n, static_cast<uint32_t>(d),
-                                                                                 sc.sums);
-        column_mean_kernel<<<static_cast<uint32_t>((d + 255) / 256), 256, 0, st>>>(sc.sums, n, static_cast<uint32_t>(d),
-                                                                                  sc.mu);
+        column_sum_kernel<<<static_cast<uint32_t>((z.n_b + 255) / 256), 256, 0, st>>>(z.b, z.n_b,
+                                                                                     static_cast<uint32_t>(d), sc.sums);
+        column_mean_kernel<<<static_cast<uint32_t>((d + 255) / 256), 256, 0, st>>>(sc.sums, z.n_b,
+                                                                                  static_cast<uint32_t>(d), sc.mu);
         launches += 2;
     }
     {
-        const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((n + 7) / 8, 148ull * 16));
-        split_bf16_kernel<<<blocks, 256, 0, st>>>(x, n, static_cast<uint32_t>(d), static_cast<uint32_t>(pitch),
+        // R = max |r'| over the base rows only (the proof's bound).
+        const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((z.n_b + 7) / 8, 148ull * 16));
+        split_bf16_kernel<<<blocks, 256, 0, st>>>(z.b, z.n_b, static_cast<uint32_t>(d), static_cast<uint32_t>(pitch),
                                                   metric == 0 ? sc.mu : nullptr, sc.hi, sc.lo, sc.norms,
                                                   sc.max_norm_bits);
         KNNG_CUDA(cudaGetLastError());
         launches += 1;
+        if (separate) {
+            // The queries' planes; their maximum norm goes to a throwaway slot.
+            const uint32_t qb = static_cast<uint32_t>(std::min<uint64_t>((z.n_q + 7) / 8, 148ull * 16));
+            split_bf16_kernel<<<qb, 256, 0, st>>>(z.q, z.n_q, static_cast<uint32_t>(d), static_cast<uint32_t>(pitch),
+                                                  metric == 0 ? sc.mu : nullptr, sc.q_hi, sc.q_lo, sc.q_norms,
+                                                  sc.counters + 3);
+            KNNG_CUDA(cudaGetLastError());
+            launches += 1;
+        }
     }
     // Candidate filter on the tensor cores.
     TcMaps m;
-    KNNG_TRY(make_map(&m.b0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sc.hi, n, pitch, pitch * 2));
-    KNNG_TRY(make_map(&m.b1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sc.lo, n, pitch, pitch * 2));
-    m.q0 = m.b0;
-    m.q1 = m.b1;
+    KNNG_TRY(make_map(&m.b0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sc.hi, z.n_b, pitch, pitch * 2));
+    KNNG_TRY(make_map(&m.b1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sc.lo, z.n_b, pitch, pitch * 2));
+    if (separate) {
+        KNNG_TRY(make_map(&m.q0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sc.q_hi, z.n_q, pitch, pitch * 2));
+        KNNG_TRY(make_map(&m.q1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sc.q_lo, z.n_q, pitch, pitch * 2));
+    } else {
+        m.q0 = m.b0;
+        m.q1 = m.b1;
+    }
     KnnTcParams p{};
     p.base_norms = sc.norms;
-    p.n_base = n;
-    p.base_id0 = 0;
-    p.n_queries = static_cast<uint32_t>(q_count);
-    p.query_row0 = static_cast<uint32_t>(q_begin);
-    p.query_id0 = static_cast<uint32_t>(q_begin);
-    p.exclude_self = 1;
+    p.n_base = z.n_b;
+    p.base_id0 = static_cast<uint32_t>(z.b_id0);
+    p.n_queries = static_cast<uint32_t>(z.n_q);
+    p.query_row0 = separate ? 0u : static_cast<uint32_t>(z.q_row_in_b);
+    p.query_id0 = static_cast<uint32_t>(z.q_id0);
+    p.exclude_self = z.exclude_self;
     p.k = static_cast<uint32_t>(c);
     p.kchunks = kchunks;
     p.out_ids = sc.cand_ids;
     p.out_keys = sc.cand_keys;
     p.error = reinterpret_cast<int*>(sc.counters + 1);
-    if (const char* dbg = std::getenv("KNNG_GPU_DEBUG_FLAGS")) p.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
+    if (const char* dbg = experiment_knob("KNNG_GPU_DEBUG_FLAGS")) p.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
     bool a_stream = false;
     p.stages = pick_stages(2, 1, false, kchunks);
     if (p.stages < 2) {
@@ -827,23 +996,29 @@ knng_gpu_status knn_f32_impl(const float* x, uint64_t n, uint64_t d, uint64_t q_
     }
     if (p.stages < 2) return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: shared memory budget exceeded");
     knng_gpu_status s;
+    EventTimer tt(stats != nullptr, 4);
+    tt.start(st);
     if (a_stream)
         s = metric == 0 ? launch_bf16_k<true, 0>(m, p, st) : launch_bf16_k<true, 1>(m, p, st);
     else
         s = metric == 0 ? launch_bf16_k<false, 0>(m, p, st) : launch_bf16_k<false, 1>(m, p, st);
+    tt.stop(st);
     KNNG_TRY(s);
     // Exact re-rank of the candidates with the proof of exactness.
     RerankParams r{};
-    r.x = x;
+    r.x = z.b;
+    r.qx = z.q;
     r.d = d;
-    r.n = n;
-    r.q_begin = static_cast<uint32_t>(q_begin);
-    r.n_queries = static_cast<uint32_t>(q_count);
+    r.n_b = z.n_b;
+    r.base_id0 = static_cast<uint32_t>(z.b_id0);
+    r.query_id0 = static_cast<uint32_t>(z.q_id0);
+    r.exclude_self = z.exclude_self;
+    r.n_queries = static_cast<uint32_t>(z.n_q);
     r.c = static_cast<uint32_t>(c);
     r.k = static_cast<uint32_t>(k);
     r.cand_ids = sc.cand_ids;
     r.cand_keys = sc.cand_keys;
-    r.norms = sc.norms;
+    r.q_norms = separate ? sc.q_norms : sc.norms + z.q_row_in_b;
     r.max_norm_bits = sc.max_norm_bits;
     r.gamma = f32_gamma(d, metric);
     r.out_ids = ids;
@@ -852,11 +1027,9 @@ knng_gpu_status knn_f32_impl(const float* x, uint64_t n, uint64_t d, uint64_t q_
     r.fallback_count = sc.counters;
     r.err_ratio_bits = sc.counters + 2;
     {
-        const uint32_t warps = 32 * kRerankWarps;
-        const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((q_count + kRerankWarps - 1) / kRerankWarps,
+        const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((z.n_q + kRerankWarps - 1) / kRerankWarps,
                                                                          148ull * 8));
         const uint32_t cpl = static_cast<uint32_t>((c + 31) / 32);
-        (void)warps;
         if (cpl <= 2)
             metric == 0 ? rerank_kernel<0, 2><<<blocks, 32 * kRerankWarps, 0, st>>>(r)
                         : rerank_kernel<1, 2><<<blocks, 32 * kRerankWarps, 0, st>>>(r);
@@ -873,31 +1046,35 @@ knng_gpu_status knn_f32_impl(const float* x, uint64_t n, uint64_t d, uint64_t q_
     // Rows the proof could not certify: exact kernel on the original rows.
     tf.start(st);
     KnnExactParams<float> e{};
-    e.base = x;
+    e.base = z.b;
     e.base_stride = d;
-    e.n_base = n;
-    e.queries = x + q_begin * d;
+    e.n_base = z.n_b;
+    e.base_id0 = static_cast<uint32_t>(z.b_id0);
+    e.queries = z.q;
     e.query_stride = d;
-    e.n_queries = static_cast<uint32_t>(q_count);
-    e.query_id0 = static_cast<uint32_t>(q_begin);
-    e.exclude_self = 1;
+    e.n_queries = static_cast<uint32_t>(z.n_q);
+    e.query_id0 = static_cast<uint32_t>(z.q_id0);
+    e.exclude_self = z.exclude_self;
     e.d = static_cast<uint32_t>(d);
     e.k = static_cast<uint32_t>(k);
     e.row_list = sc.fallback_rows;
     e.row_count = sc.counters;
     e.out_ids = ids;
     e.out_dists = dists;
-    KNNG_TRY(launch_exact(e, metric, static_cast<uint32_t>(q_count), st));
+    KNNG_TRY(launch_exact(e, metric, static_cast<uint32_t>(z.n_q), st));
     tf.stop(st);
     launches += 1;
-    uint32_t host_counters[2] = {0, 0};
-    KNNG_TRY(read_counters(sc.counters, host_counters, st));
-    uint32_t ratio_bits = 0;
-    KNNG_CUDA(cudaMemcpy(&ratio_bits, sc.counters + 2, 4, cudaMemcpyDeviceToHost));
+    uint32_t host_counters[3] = {0, 0, 0};
+    KNNG_CUDA(cudaMemcpyAsync(host_counters, sc.counters, 12, cudaMemcpyDeviceToHost, st));
+    KNNG_CUDA(cudaStreamSynchronize(st));
+    if (host_counters[1] != 0)
+        return fail(KNNG_GPU_TIMEOUT, "knng::gpu: a bounded device wait gave up (code " +
+                                          std::to_string(host_counters[1]) + ")");
     if (stats) {
         float ratio;
-        std::memcpy(&ratio, &ratio_bits, 4);
+        std::memcpy(&ratio, &host_counters[2], 4);
         stats->f32_err_ratio = ratio;
+        stats->tc_ms = tt.ms();
         stats->path = KNNG_PATH_F32_TENSOR;
         stats->fallback_rows = host_counters[0];
         stats->knn_ms = tk.ms();
@@ -905,6 +1082,45 @@ knng_gpu_status knn_f32_impl(const float* x, uint64_t n, uint64_t d, uint64_t q_
         stats->kernel_launches += launches;
     }
     return KNNG_GPU_OK;
+}
+
+knng_gpu_status knn_f32_impl(const float* x, uint64_t n, uint64_t d, uint64_t q_begin, uint64_t q_count, uint64_t k,
+                             int metric, uint32_t* ids, float* dists, void* scratch, uint64_t scratch_bytes,
+                             cudaStream_t st, knng_gpu_stats* stats)
+{
+    if (q_begin + q_count > n) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: query range exceeds the base");
+    const F32Sets z{x + q_begin * d, q_count, q_begin, x, n, 0, 1, static_cast<int64_t>(q_begin)};
+    return knn_f32_sets_impl(z, d, k, metric, ids, dists, scratch, scratch_bytes, st, stats);
+}
+
+// Recall of an approximate graph against the true one
+// (src/bench/recall.cpp:52-96): per row, the distinct ids of the approximate
+// row that also appear in the true row; a repeated approximate id counts
+// once. One warp per row; lane l looks at entries l, l + 32, ...
+__global__ void __launch_bounds__(256) recall_hits_kernel(const uint32_t* __restrict__ approx,
+                                                          const uint32_t* __restrict__ truth, uint64_t n, uint32_t k,
+                                                          unsigned long long* __restrict__ hits)
+{
+    const uint32_t lane = threadIdx.x & 31;
+    const uint64_t warp0 = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = (static_cast<uint64_t>(gridDim.x) * blockDim.x) >> 5;
+    unsigned long long local = 0;
+    for (uint64_t r = warp0; r < n; r += nwarps) {
+        const uint32_t* a = approx + r * k;
+        const uint32_t* t = truth + r * k;
+        for (uint32_t j = lane; j < k; j += 32) {
+            const uint32_t id = a[j];
+            bool first = true;
+            for (uint32_t i = 0; i < j && first; ++i) first = a[i] != id;
+            if (!first) continue;
+            bool found = false;
+            for (uint32_t i = 0; i < k && !found; ++i) found = t[i] == id;
+            local += found ? 1ull : 0ull;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+    if (lane == 0 && local) atomicAdd(hits, local);
 }
 
 struct WorkspaceLayout {
@@ -920,7 +1136,7 @@ WorkspaceLayout workspace_layout(uint64_t n, uint64_t d, uint64_t k)
     w.norms = align_up(w.packed + n * pitch, 256);
     w.flag = align_up(w.norms + n * 4, 256);
     w.scratch = w.flag + 256;
-    const uint64_t u8_total = w.scratch + scratch_u8_bytes(n);
+    const uint64_t u8_total = w.scratch + scratch_u8_bytes(n, k);
     const uint64_t f32_total = w.scratch + layout_scratch_f32(nullptr, n, d, n, k).total;
     w.total = std::max(u8_total, f32_total);
     return w;
@@ -974,7 +1190,7 @@ knng_gpu_status device_pipeline_u8(const uint8_t* rows_u8, uint64_t n, uint64_t 
     uint8_t* base = static_cast<uint8_t*>(ws);
     uint8_t* packed = base + w.packed;
     int32_t* norms = reinterpret_cast<int32_t*>(base + w.norms);
-    EventTimer tall(stats != nullptr), tp(stats != nullptr);
+    EventTimer tall(stats != nullptr, 0), tp(stats != nullptr, 1);
     tall.start(st);
     tp.start(st);
     KNNG_TRY(pack_bytes_impl(rows_u8, n, d, row_stride, packed, norms, st));
@@ -1005,25 +1221,40 @@ knng_gpu_status device_pipeline(const float* x, uint64_t n, uint64_t d, uint64_t
     uint8_t* packed = base + w.packed;
     int32_t* norms = reinterpret_cast<int32_t*>(base + w.norms);
     int32_t* flag = reinterpret_cast<int32_t*>(base + w.flag);
-    EventTimer tall(stats != nullptr), tp(stats != nullptr);
+    EventTimer tall(stats != nullptr, 0), tp(stats != nullptr, 1);
     tall.start(st);
     tp.start(st);
     KNNG_CUDA(cudaMemsetAsync(flag, 0, 4, st));
     KNNG_TRY(pack_impl(x, n, d, packed, norms, flag, st));
     tp.stop(st);
-    int32_t nonint = 0;
-    KNNG_CUDA(cudaMemcpyAsync(&nonint, flag, 4, cudaMemcpyDeviceToHost, st));
-    KNNG_CUDA(cudaStreamSynchronize(st));
     if (stats) {
         std::memset(stats, 0, sizeof(*stats));
         stats->kernel_launches = 2;  // pack + augmentation
     }
+    const U8Sets z{packed, norms, n, 0, packed, norms, n, 0, 1};
+    U8RunOptions opt;
+    opt.skip_flag = flag;
+    const bool pair = pair_applies(z, d, k, metric, carve_scratch_u8(base + w.scratch, n, k, w.total - w.scratch), opt);
+    int32_t nonint = 0;
+    if (!pair) {
+        // The single-CTA kernel cannot skip itself: read the flag first.
+        KNNG_CUDA(cudaMemcpyAsync(&nonint, flag, 4, cudaMemcpyDeviceToHost, st));
+        KNNG_CUDA(cudaStreamSynchronize(st));
+    }
     if (nonint == 0) {
+        // The pair kernel returns at once when the flag is set; the flag is
+        // read after it, together with its counters.
         KNNG_TRY(knn_u8_impl(packed, norms, n, d, 0, n, k, metric, ids, dists, base + w.scratch, w.total - w.scratch,
-                             st, stats));
-    } else {
+                             st, stats, opt));
+        if (pair) {
+            KNNG_CUDA(cudaMemcpyAsync(&nonint, flag, 4, cudaMemcpyDeviceToHost, st));
+            KNNG_CUDA(cudaStreamSynchronize(st));
+        }
+    }
+    if (nonint != 0) {
         // The packed bytes are meaningless for such data; the fp32 path
         // reuses the whole workspace.
+        if (stats) stats->kernel_launches = 2;
         KNNG_TRY(knn_f32_impl(x, n, d, 0, n, k, metric, ids, dists, base, w.total, st, stats));
     }
     tall.stop(st);
@@ -1040,29 +1271,75 @@ knng_gpu_status device_pipeline(const float* x, uint64_t n, uint64_t d, uint64_t
 // Scratch of knng_gpu_knn_u8_noalloc: the fallback-row list for up to
 // KNNG_GPU_NOALLOC_MAX_QUERIES queries plus the counters. Host code must not
 // pass `g_noalloc_scratch` itself to a kernel (on the host it names a host
-// stand-in); noalloc_scratch_ptr() resolves the device address once per device.
+// stand-in); noalloc_scratch_ptr() resolves the device address.
 constexpr uint64_t kNoAllocScratchBytes = (static_cast<uint64_t>(KNNG_GPU_NOALLOC_MAX_QUERIES) * 4 + 255) / 256 * 256 + 256;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
-constexpr int kMaxDevices = 64;
+// The address of a __device__ array belongs to a CUDA context, not to a
+// device number: a host may make a non-primary context current. The cache
+// is therefore keyed by the current context (driver entry point
+// cuCtxGetCurrent) and emptied by knng_gpu_release_cached_buffers.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+constexpr int kNoAllocSlots = 64;
 std::mutex g_noalloc_mutex;
-void* g_noalloc_ptr[kMaxDevices] = {};
+CUcontext g_noalloc_ctx[kNoAllocSlots] = {};
+void* g_noalloc_ptr[kNoAllocSlots] = {};
+
+knng_gpu_status current_context(CUcontext* out)
+{
+    static CtxGetCurrentFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p)
+            return fail(KNNG_GPU_CUDA_ERROR, "knng::gpu: cuCtxGetCurrent entry point not available");
+        fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    }
+    if (fn(out) != CUDA_SUCCESS) return fail(KNNG_GPU_CUDA_ERROR, "knng::gpu: cuCtxGetCurrent failed");
+    return KNNG_GPU_OK;
+}
 
 knng_gpu_status noalloc_scratch_ptr(void** out)
 {
     int dev = 0;
     KNNG_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= kMaxDevices) return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: device index out of range");
-    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (!g_noalloc_ptr[dev]) {
-        void* ptr = nullptr;
-        // The current device is `dev`, so this resolves that device's copy.
-        KNNG_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
-        g_noalloc_ptr[dev] = ptr;
+    CUcontext ctx = nullptr;
+    KNNG_TRY(current_context(&ctx));
+    if (!ctx) {
+        // No context current yet: the runtime call makes the device's
+        // primary context current.
+        void* probe = nullptr;
+        KNNG_CUDA(cudaGetSymbolAddress(&probe, g_noalloc_scratch));
+        KNNG_TRY(current_context(&ctx));
     }
-    *out = g_noalloc_ptr[dev];
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    for (int i = 0; i < kNoAllocSlots; ++i)
+        if (g_noalloc_ctx[i] == ctx && g_noalloc_ptr[i]) {
+            *out = g_noalloc_ptr[i];
+            return KNNG_GPU_OK;
+        }
+    void* ptr = nullptr;
+    // With this context current, the symbol resolves to its copy of the array.
+    KNNG_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+    for (int i = 0; i < kNoAllocSlots; ++i)
+        if (!g_noalloc_ptr[i]) {
+            g_noalloc_ctx[i] = ctx;
+            g_noalloc_ptr[i] = ptr;
+            break;
+        }
+    *out = ptr;
     return KNNG_GPU_OK;
+}
+
+void noalloc_forget_all()
+{
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    for (int i = 0; i < kNoAllocSlots; ++i) {
+        g_noalloc_ctx[i] = nullptr;
+        g_noalloc_ptr[i] = nullptr;
+    }
 }
 }  // namespace
 
@@ -1115,7 +1392,7 @@ uint64_t knng_gpu_knn_f32_scratch_bytes(uint64_t n, uint64_t d, uint64_t q_count
     return layout_scratch_f32(nullptr, n, d, q_count, k).total;
 }
 
-uint64_t knng_gpu_knn_scratch_bytes(uint64_t q_count) { return scratch_u8_bytes(q_count); }
+uint64_t knng_gpu_knn_scratch_bytes(uint64_t q_count, uint64_t k) { return scratch_u8_bytes(q_count, k); }
 
 knng_gpu_status knng_gpu_pack_u8(const float* d_x, uint64_t rows, uint64_t d, uint8_t* d_packed, int32_t* d_norms,
                                  int32_t* d_nonint, void* stream)
@@ -1255,6 +1532,7 @@ void knng_gpu_release_cached_buffers(void)
     }
     if (have_cur) cudaSetDevice(cur);
     cudaGetLastError();
+    noalloc_forget_all();
 }
 
 knng_gpu_status knng_gpu_knn_u8_noalloc(const uint8_t* d_packed, const int32_t* d_norms, uint64_t n, uint64_t d,
@@ -1270,10 +1548,64 @@ knng_gpu_status knng_gpu_knn_u8_noalloc(const uint8_t* d_packed, const int32_t* 
     void* scratch = nullptr;
     KNNG_TRY(noalloc_scratch_ptr(&scratch));
     // knn_u8_impl zeroes the counters on `stream` before the kernel runs, so
-    // the previous call's contents never leak into this one.
-    // No tail split here: it would create streams and events.
+    // the previous call's contents never leak into this one. The array has
+    // no room for the pair kernel's partial lists, so the single-CTA kernel
+    // runs; no timing events are recorded (the *_ms fields of stats stay 0).
+    U8RunOptions opt;
+    opt.allow_pair = false;
+    opt.timing = false;
+    if (stats) std::memset(stats, 0, sizeof(*stats));
     return knn_u8_impl(d_packed, d_norms, n, d, q_begin, q_count, k, metric, d_ids, d_dists, scratch,
-                       kNoAllocScratchBytes, static_cast<cudaStream_t>(stream), stats, false);
+                       kNoAllocScratchBytes, static_cast<cudaStream_t>(stream), stats, opt);
+}
+
+knng_gpu_status knng_gpu_selftest_bounded_wait(uint64_t wait_limit_cycles)
+{
+    g_last_error.clear();
+    // A small, valid build (every row of bytes 1..n) whose pair kernel runs
+    // with the given wait bound while the leader CTAs withhold the arrival
+    // of their first stage: the MMA waits give up, the kernel unwinds and
+    // frees its TMEM, and the call must report KNNG_GPU_TIMEOUT.
+    const uint64_t n = 4096, d = 128, k = 10;
+    const uint64_t pitch = knng_gpu_padded_dim(d);
+    uint8_t *rows = nullptr, *packed = nullptr, *scratch = nullptr;
+    int32_t* norms = nullptr;
+    uint32_t* ids = nullptr;
+    float* dists = nullptr;
+    const uint64_t sbytes = scratch_u8_bytes(n, k);
+    struct Free {
+        void* p[6];
+        ~Free()
+        {
+            for (void* q : p)
+                if (q) cudaFree(q);
+        }
+    } guard{};
+    KNNG_CUDA(cudaMalloc(&rows, n * d));
+    guard.p[0] = rows;
+    KNNG_CUDA(cudaMalloc(&packed, n * pitch));
+    guard.p[1] = packed;
+    KNNG_CUDA(cudaMalloc(&norms, n * 4));
+    guard.p[2] = norms;
+    KNNG_CUDA(cudaMalloc(&ids, n * k * 4));
+    guard.p[3] = ids;
+    KNNG_CUDA(cudaMalloc(&dists, n * k * 4));
+    guard.p[4] = dists;
+    KNNG_CUDA(cudaMalloc(&scratch, sbytes));
+    guard.p[5] = scratch;
+    KNNG_CUDA(cudaMemset(rows, 1, n * d));
+    KNNG_TRY(pack_bytes_impl(rows, n, d, d, packed, norms, nullptr));
+    U8RunOptions opt;
+    opt.wait_limit = static_cast<long long>(std::min<uint64_t>(wait_limit_cycles, 1ull << 40));
+    opt.test_mode = 1;
+    opt.timing = false;
+    const U8Sets z{packed, norms, n, 0, packed, norms, n, 0, 1};
+    ScratchU8 sc = carve_scratch_u8(scratch, n, k, sbytes);
+    if (!pair_applies(z, d, k, 0, sc, opt))
+        return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: the pair kernel does not apply on this device");
+    const knng_gpu_status s = knn_u8_sets_impl(z, d, k, 0, ids, dists, scratch, sbytes, nullptr, nullptr, opt);
+    KNNG_CUDA(cudaDeviceSynchronize());
+    return s;
 }
 
 knng_gpu_status knng_gpu_knn_u8_sets(const uint8_t* d_q_packed, const int32_t* d_q_norms, uint64_t n_q,
@@ -1296,6 +1628,58 @@ knng_gpu_status knng_gpu_knn_u8_sets(const uint8_t* d_q_packed, const int32_t* d
                             static_cast<cudaStream_t>(stream), stats);
 }
 
+uint64_t knng_gpu_knn_f32_sets_scratch_bytes(uint64_t n_q, uint64_t n_b, uint64_t d, uint64_t k, int exclude_self)
+{
+    if (n_b == 0) return 256;
+    return layout_scratch_f32_sets(nullptr, n_b, n_q, d, k, exclude_self ? 1 : 0, true).total;
+}
+
+knng_gpu_status knng_gpu_knn_f32_sets(const float* d_q, uint64_t n_q, uint64_t q_id0, const float* d_b, uint64_t n_b,
+                                      uint64_t b_id0, uint64_t d, uint64_t k, int metric, int exclude_self,
+                                      uint32_t* d_ids, float* d_dists, void* d_scratch, uint64_t scratch_bytes,
+                                      void* stream, knng_gpu_stats* stats)
+{
+    g_last_error.clear();
+    if (k == 0) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu::brute_force_knn: k must be > 0");
+    if (k > KNNG_GPU_MAX_K)
+        return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: k exceeds the GPU limit " + std::to_string(KNNG_GPU_MAX_K));
+    if (metric != KNNG_METRIC_L2_SQUARED && metric != KNNG_METRIC_NEGATIVE_INNER_PRODUCT)
+        return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: unknown metric id " + std::to_string(metric));
+    if (d == 0 || n_b == 0) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: empty base");
+    if (d > (1u << 20)) return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: d must be in [1, 2^20]");
+    if (q_id0 + n_q > 0xFFFFFFFFull || b_id0 + n_b > 0xFFFFFFFFull)
+        return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: ids exceed the 32-bit index_t range");
+    const F32Sets z{d_q, n_q, q_id0, d_b, n_b, b_id0, exclude_self ? 1 : 0, -1};
+    if (stats) std::memset(stats, 0, sizeof(*stats));
+    return knn_f32_sets_impl(z, d, k, metric, d_ids, d_dists, d_scratch, scratch_bytes,
+                             static_cast<cudaStream_t>(stream), stats);
+}
+
+knng_gpu_status knng_gpu_recall_at_k(const uint32_t* d_approx, const uint32_t* d_truth, uint64_t n, uint64_t k,
+                                     void* d_counter, void* stream, double* recall)
+{
+    g_last_error.clear();
+    if (!recall) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::bench::recall: recall is NULL");
+    if (n == 0) {
+        *recall = 1.0;  // src/bench/recall.cpp: an empty graph has recall 1
+        return KNNG_GPU_OK;
+    }
+    if (k == 0 || k > 0xFFFFFFFFull) return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::bench::recall: bad k");
+    if (!d_counter || (reinterpret_cast<uintptr_t>(d_counter) & 7))
+        return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::bench::recall: d_counter must be 8 device bytes, 8-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    auto* hits = static_cast<unsigned long long*>(d_counter);
+    KNNG_CUDA(cudaMemsetAsync(hits, 0, 8, st));
+    const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((n + 7) / 8, 148ull * 32));
+    recall_hits_kernel<<<blocks, 256, 0, st>>>(d_approx, d_truth, n, static_cast<uint32_t>(k), hits);
+    KNNG_CUDA(cudaGetLastError());
+    unsigned long long h = 0;
+    KNNG_CUDA(cudaMemcpyAsync(&h, hits, 8, cudaMemcpyDeviceToHost, st));
+    KNNG_CUDA(cudaStreamSynchronize(st));
+    *recall = static_cast<double>(h) / (static_cast<double>(n) * static_cast<double>(k));
+    return KNNG_GPU_OK;
+}
+
 knng_gpu_status knng_gpu_merge_topk(const uint32_t* d_a_ids, const float* d_a_dists, const uint32_t* d_b_ids,
                                     const float* d_b_dists, uint64_t rows, uint64_t k, uint32_t* d_out_ids,
                                     float* d_out_dists, void* stream)
@@ -1309,3 +1693,6 @@ knng_gpu_status knng_gpu_merge_topk(const uint32_t* d_a_ids, const float* d_a_di
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ multi-GPU builds
+#include "sharded.cuh"

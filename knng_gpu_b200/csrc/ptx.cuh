@@ -1,7 +1,7 @@
 // ptx.cuh -- inline-PTX helpers for sm_100a: mbarriers, TMA tile loads,
 // tcgen05 (TMEM alloc, UMMA issue/commit, TMEM loads) and bounded waits.
 //
-// Every wait here is bounded: after `kSpinLimitCycles` of failed polling the
+// Every wait here is bounded: after `limit` cycles (default kSpinLimitCycles) of failed polling the
 // helper returns false, the caller records an error code in device memory and
 // unwinds. No kernel of this library spins forever.
 #pragma once
@@ -87,7 +87,8 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity)
 
 // Same bound as mbar_wait, polling with the non-suspending test_wait (for
 // the single-thread producer / MMA roles, where wake-up latency matters).
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort)
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                               long long limit = kSpinLimitCycles)
 {
     if (mbar_test_wait(bar, parity)) return true;
     const long long t0 = clock64();
@@ -95,14 +96,15 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, v
         if (mbar_test_wait(bar, parity)) return true;
         if ((it & 1023u) == 0) {
             if (*abort) return false;
-            if (clock64() - t0 > kSpinLimitCycles) return false;
+            if (clock64() - t0 > limit) return false;
         }
     }
 }
 
 // Wait for the phase with the given parity to complete. Returns false after
 // kSpinLimitCycles, or early when *abort becomes non-zero.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort)
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          long long limit = kSpinLimitCycles)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
@@ -110,14 +112,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 255u) == 0) {
             if (*abort) return false;
-            if (clock64() - t0 > kSpinLimitCycles) return false;
+            if (clock64() - t0 > limit) return false;
         }
     }
 }
 
 // mbar_wait for the single-thread roles: suspended in the barrier between
 // polls (hint ~0.1 ms), so a waiting producer / MMA thread takes no issue slots.
-__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort)
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                long long limit = kSpinLimitCycles)
 {
     if (mbar_try_wait_hint(bar, parity, 100000u)) return true;
     const long long t0 = clock64();
@@ -125,14 +128,24 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
         if (mbar_try_wait_hint(bar, parity, 100000u)) return true;
         if ((it & 15u) == 0) {
             if (*abort) return false;
-            if (clock64() - t0 > kSpinLimitCycles) return false;
+            if (clock64() - t0 > limit) return false;
         }
     }
 }
 
+// Bounded wait that ignores the abort flag (draining copies in flight
+// after an abort).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, long long limit)
+{
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > limit) return false;
+    return true;
+}
+
 // Bounded wait until a shared-memory counter reaches `target`.
 __device__ __forceinline__ bool spin_until_geq(volatile uint32_t* counter, uint32_t target, volatile int* abort,
-                                               uint32_t sleep_ns = 32)
+                                               uint32_t sleep_ns = 32, long long limit = kSpinLimitCycles)
 {
     if (*counter >= target) return true;
     const long long t0 = clock64();
@@ -140,7 +153,7 @@ __device__ __forceinline__ bool spin_until_geq(volatile uint32_t* counter, uint3
         if (*counter >= target) return true;
         if ((it & 255u) == 0) {
             if (*abort) return false;
-            if (clock64() - t0 > kSpinLimitCycles) return false;
+            if (clock64() - t0 > limit) return false;
         }
         __nanosleep(sleep_ns);
     }
@@ -308,6 +321,105 @@ __device__ __forceinline__ void tmem_ld_wait_n(int32_t* v)
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthreads)
 {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------- CTA pairs (cluster of 2)
+// Rank of this CTA in its cluster.
+__device__ __forceinline__ uint32_t cluster_ctarank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// shared::cluster address of the object at local shared address `saddr` in
+// the CTA of cluster rank `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+
+// Arrive (release, cluster scope) on an mbarrier given by its shared::cluster
+// address, possibly in the peer CTA.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
+{
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v)
+{
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+// All threads of both CTAs of the pair.
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// TMA tile load into this CTA's shared memory whose completion is counted on
+// an mbarrier of the pair's leader CTA (`bar_cluster` = shared::cluster
+// address). No multicast: each CTA fetches only its own rows.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                                 uint32_t bar_cluster)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3}], [%4];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+
+// 1-D TMA tile load (local barrier).
+__device__ __forceinline__ void tma_load_1d(void* smem_dst, const CUtensorMap* map, int32_t x, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.1d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2}], [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// TMEM allocation shared by the CTA pair: one warp of each CTA (same warp
+// index) executes it; both receive the same column address.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Pair UMMA (issued by the leader CTA only): D[256 x N] over both CTAs' TMEM,
+// A = 128 rows from each CTA, B = N/2 rows from each CTA, at the same
+// shared-memory offsets in both.
+__device__ __forceinline__ void umma_u8_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Completion of the pair UMMAs issued so far, signalled on the mbarrier at
+// the same shared-memory offset in both CTAs of the pair.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar)
+{
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(static_cast<uint16_t>(3))
+        : "memory");
 }
 
 }  // namespace knng_b200

@@ -47,55 +47,78 @@ static uint64_t xs_below(uint64_t *s, uint64_t bound)
     return (uint64_t)(p >> 64);
 }
 
+/* One row of recipe `kind` from the stream `s` (kinds 0, 2, 3, 4; kind 1
+ * with its centres in `centres`). */
+static void gen_row(int kind, uint64_t *s, uint64_t d, float *row, const float *centres, uint64_t components,
+                    float sigma, float p_zero)
+{
+    switch (kind) {
+    case 0:
+        for (uint64_t j = 0; j < d; ++j) row[j] = (float)xs_below(s, 256);
+        break;
+    case 1: {
+        const double two_pi = 6.283185307179586476925286766559;
+        const float *c = centres + xs_below(s, components) * d;
+        for (uint64_t j = 0; j < d; ++j) {
+            const double u1 = (double)xs_float01(s);
+            const double u2 = (double)xs_float01(s);
+            const float z = (float)(sqrt(-2.0 * log(1.0 - u1)) * cos(two_pi * u2));
+            row[j] = c[j] + sigma * z;
+        }
+        break;
+    }
+    case 2: {
+        float acc = 0.0f;
+        for (uint64_t j = 0; j < d; ++j) {
+            row[j] = xs_float01(s);
+            const float sq = row[j] * row[j];
+            acc = acc + sq;
+        }
+        const float norm = sqrtf(acc);
+        if (norm > 0.0f)
+            for (uint64_t j = 0; j < d; ++j) row[j] = row[j] / norm;
+        break;
+    }
+    case 3:
+        for (uint64_t j = 0; j < d; ++j) row[j] = xs_float01(s) < p_zero ? 0.0f : (float)(1 + xs_below(s, 255));
+        break;
+    default: /* 4 */
+        for (uint64_t j = 0; j < d; ++j) row[j] = 2.0f * xs_float01(s) - 1.0f;
+        break;
+    }
+}
+
+/* Rows [row_begin, row_begin + row_count) of the dataset of `kind` (the
+ * same values as the full dataset holds there; the stream is advanced over
+ * the rows before). Returns 0 on success, -1 for an unknown kind, a zero
+ * seed or missing scratch. `scratch` must hold components*d floats for kind
+ * 1 plus d floats (d floats for the other kinds; may be NULL when
+ * row_begin == 0 and kind != 1). */
+int knng_synth_generate_rows(int kind, uint64_t seed, uint64_t row_begin, uint64_t row_count, uint64_t d, float *out,
+                             uint64_t components, float sigma, float p_zero, float *scratch)
+{
+    if (seed == 0 || kind < 0 || kind > 4) return -1;
+    if ((kind == 1 && (!scratch || components == 0)) || (row_begin > 0 && !scratch)) return -1;
+    uint64_t s = seed;
+    const float *centres = NULL;
+    float *skip_row = scratch;
+    if (kind == 1) {
+        for (uint64_t i = 0; i < components * d; ++i) scratch[i] = 2.0f * xs_float01(&s) - 1.0f;
+        centres = scratch;
+        skip_row = scratch + components * d;
+    }
+    for (uint64_t r = 0; r < row_begin; ++r) gen_row(kind, &s, d, skip_row, centres, components, sigma, p_zero);
+    for (uint64_t r = 0; r < row_count; ++r) gen_row(kind, &s, d, out + r * d, centres, components, sigma, p_zero);
+    return 0;
+}
+
 /* Returns 0 on success, -1 for an unknown kind or a zero seed. `scratch`
  * must hold components*d floats for kind 1 (may be NULL otherwise). */
 int knng_synth_generate(int kind, uint64_t seed, uint64_t n, uint64_t d, float *out, uint64_t components,
                         float sigma, float p_zero, float *scratch)
 {
-    if (seed == 0) return -1;
-    uint64_t s = seed;
-    switch (kind) {
-    case 0:
-        for (uint64_t i = 0; i < n * d; ++i) out[i] = (float)xs_below(&s, 256);
-        return 0;
-    case 1: {
-        if (!scratch || components == 0) return -1;
-        for (uint64_t i = 0; i < components * d; ++i) scratch[i] = 2.0f * xs_float01(&s) - 1.0f;
-        const double two_pi = 6.283185307179586476925286766559;
-        for (uint64_t r = 0; r < n; ++r) {
-            const float *c = scratch + xs_below(&s, components) * d;
-            for (uint64_t j = 0; j < d; ++j) {
-                const double u1 = (double)xs_float01(&s);
-                const double u2 = (double)xs_float01(&s);
-                const float z = (float)(sqrt(-2.0 * log(1.0 - u1)) * cos(two_pi * u2));
-                out[r * d + j] = c[j] + sigma * z;
-            }
-        }
-        return 0;
-    }
-    case 2:
-        for (uint64_t r = 0; r < n; ++r) {
-            float *row = out + r * d;
-            float acc = 0.0f;
-            for (uint64_t j = 0; j < d; ++j) {
-                row[j] = xs_float01(&s);
-                const float sq = row[j] * row[j];
-                acc = acc + sq;
-            }
-            const float norm = sqrtf(acc);
-            if (norm > 0.0f)
-                for (uint64_t j = 0; j < d; ++j) row[j] = row[j] / norm;
-        }
-        return 0;
-    case 3:
-        for (uint64_t i = 0; i < n * d; ++i) out[i] = xs_float01(&s) < p_zero ? 0.0f : (float)(1 + xs_below(&s, 255));
-        return 0;
-    case 4:
-        for (uint64_t i = 0; i < n * d; ++i) out[i] = 2.0f * xs_float01(&s) - 1.0f;
-        return 0;
-    default:
-        return -1;
-    }
+    if (kind == 1 && (!scratch || components == 0)) return -1;
+    return knng_synth_generate_rows(kind, seed, 0, n, d, out, components, sigma, p_zero, scratch);
 }
 
 /* Sorted, distinct query ids for the subset harness: ids drawn with

@@ -1,31 +1,32 @@
-"""Sharded multi-GPU build: one process per GPU, torch.distributed (NCCL) for
-the exchange steps, the C-ABI kernels for the compute.
+"""Sharded multi-GPU build, one process per GPU: a thin Python layer over the
+C-ABI sharded build (knng_gpu_brute_force_sharded, include/knng_gpu.h).
 
-Mirrors the reference's distributed brute force (src/dist/brute_force_mpi.cpp:36-142,
-include/knng/dist/sharded_dataset.hpp:145-155) with the base replicated
-instead of ring-passed:
+The library owns the NCCL communicator of each rank and every exchange step
+(all-reduce of the integer flag, all-gather of the packed base or the ring
+pass of base blocks, gather of graph rows to rank 0). torch.distributed only
+hands the NCCL unique id from rank 0 to the other ranks.
 
-1. every rank packs its slice of rows (u8 + norms + integer check) -- the
-   ``MPI_Scatterv`` of src/dist/sharded_dataset.cpp:72 becomes a local H2D
-   of the rank's slice;
-2. ``all_reduce(MAX)`` of the "not integer" flag, then ``all_gather`` of the
-   packed slices so every GPU holds the full packed base (128 MB for 1M x 128);
-3. every rank runs the fused kernel on its query shard (``compute_shard``:
-   contiguous blocks, the last rank takes the remainder) against the full base;
-4. the Knng rows are gathered to rank 0 -- the two ``MPI_Gatherv`` of
-   src/dist/brute_force_mpi.cpp:179-200 -- as one ``all_gather`` of padded
-   equal shards (NCCL has no Gatherv).
+Mirrors the reference's distributed brute force (src/dist/brute_force_mpi.cpp:36-203,
+include/knng/dist/sharded_dataset.hpp:145-155):
 
-Non-integer data takes the same steps with fp32 rows and the exact kernel.
+* query rows are sharded by ``compute_shard`` (contiguous blocks, the last
+  rank takes the remainder);
+* mode 0 replicates the packed base on every GPU (all-gather); mode 1 keeps
+  it sharded and passes the blocks around a ring while the kernel searches the
+  current block (the reference's ring of MPI_Sendrecv);
+* rank 0 receives the whole graph.
 """
 from __future__ import annotations
 
+import ctypes
+import time
 from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
 
 from . import api
+from ._native import KnngGpuStats, gpu_lib
 
 
 @dataclass(frozen=True)
@@ -45,12 +46,10 @@ SLICE_ALIGN = 256
 
 
 def slice_rows(global_n: int, num_ranks: int) -> int:
-    """Rows per rank in the equal-size slices that are packed and all-gathered:
-    ceil(n / ranks) rounded up to SLICE_ALIGN rows, so every slice starts on a
-    base-tile boundary of the fused kernel (the pack derives each 128-row
-    tile's augmentation offset from that tile alone; tiles that straddle two
-    packs stay exact but filter less sharply). Trailing ranks may get an empty
-    slice when n is small."""
+    """Rows per rank in the replicate mode's equal slices (packed and
+    all-gathered): ceil(n / ranks) rounded up to SLICE_ALIGN rows, so every
+    slice starts on a base tile of the fused kernel. Trailing ranks may get an
+    empty slice when n is small. Same rule as the library's."""
     per = (global_n + num_ranks - 1) // num_ranks
     return (per + SLICE_ALIGN - 1) // SLICE_ALIGN * SLICE_ALIGN
 
@@ -76,209 +75,177 @@ def unpad_shards(t: torch.Tensor, n: int, world: int) -> torch.Tensor:
     return torch.cat(parts, 0)
 
 
-class ShardedBuilder:
-    """Reusable buffers for repeated sharded builds of an (n, d) dataset with k
-    neighbours on this rank's GPU. All collectives run on the current stream."""
+class NcclComm:
+    """This rank's communicator inside the library (knng_gpu_comm_create).
+    The unique id travels from rank 0 over the default torch.distributed
+    group; create it with the rank's GPU current."""
 
-    def __init__(self, n: int, d: int, k: int, metric: int, group=None):
-        self.n, self.d, self.k, self.metric = n, d, k, metric
-        self.group = group
-        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
-        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+    def __init__(self, group=None):
+        lib = gpu_lib()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        nbytes = int(lib.knng_gpu_nccl_id_bytes())
+        idbuf = (ctypes.c_uint8 * nbytes)()
+        if self.rank == 0:
+            api.check(lib.knng_gpu_nccl_unique_id(idbuf))
         dev = torch.device("cuda", torch.cuda.current_device())
-        self.dev = dev
-        self.s = slice_rows(n, self.world)
-        self.pitch = api.padded_dim(d)
-        self.packed = torch.empty((self.world * self.s, self.pitch), dtype=torch.uint8, device=dev)
-        self.norms = torch.empty((self.world * self.s,), dtype=torch.int32, device=dev)
-        self.flag = torch.zeros((1,), dtype=torch.int32, device=dev)
+        t = torch.tensor(list(bytes(idbuf)), dtype=torch.uint8, device=dev)
+        dist.broadcast(t, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        idbytes = bytes(t.cpu().tolist())
+        ctypes.memmove(idbuf, idbytes, nbytes)
+        handle = ctypes.c_void_p()
+        api.check(lib.knng_gpu_comm_create(idbuf, self.world, self.rank, ctypes.byref(handle)))
+        self.handle = handle
+
+    def close(self) -> None:
+        if self.handle:
+            gpu_lib().knng_gpu_comm_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+MODE_REPLICATE = 0
+MODE_RING = 1
+
+
+class ShardedBuilder:
+    """Repeated sharded builds of an (n, d) dataset with k neighbours on this
+    rank's GPU, through the C ABI. ``mode``: MODE_REPLICATE (base all-gathered)
+    or MODE_RING (base blocks passed around the ring; integer data only).
+    ``build`` takes this rank's rows ``slice_bounds`` as CUDA float32 and
+    returns the (n, k) graph on rank 0, (None, None) on the other ranks."""
+
+    def __init__(self, n: int, d: int, k: int, metric: int, mode: int = MODE_REPLICATE, group=None):
+        self.n, self.d, self.k, self.metric, self.mode = n, d, k, metric, mode
+        self.comm = NcclComm(group)
+        self.world, self.rank = self.comm.world, self.comm.rank
+        self.dev = torch.device("cuda", torch.cuda.current_device())
+        lib = gpu_lib()
+        b, c = ctypes.c_uint64(), ctypes.c_uint64()
+        lib.knng_gpu_shard_rows(n, self.world, self.rank, mode, ctypes.byref(b), ctypes.byref(c))
+        self._slice = (int(b.value), int(b.value) + int(c.value))
         self.shard = compute_shard(n, self.world, self.rank)
-        self.max_shard = compute_shard(n, self.world, self.world - 1).count
-        self.ids = torch.empty((self.max_shard, k), dtype=torch.int32, device=dev)
-        self.dists = torch.empty((self.max_shard, k), dtype=torch.float32, device=dev)
-        self.scratch = torch.empty(api.knn_scratch_bytes(self.max_shard), dtype=torch.uint8, device=dev)
-        self.all_ids = torch.empty((self.world * self.max_shard, k), dtype=torch.int32, device=dev)
-        self.all_dists = torch.empty((self.world * self.max_shard, k), dtype=torch.float32, device=dev)
-        self.f32_full = None
-        self.f32_scratch = None
-        # Optional per-phase device timing (set .timing = True): CUDA events on
-        # the current stream; phase_ms() reads them after a build.
-        self.timing = False
-        self._marks: list = []
+        self.ws = torch.empty(int(lib.knng_gpu_sharded_workspace_bytes(n, d, k, self.world, mode)),
+                              dtype=torch.uint8, device=self.dev)
+        if self.rank == 0:
+            self.ids = torch.empty((n, k), dtype=torch.int32, device=self.dev)
+            self.dists = torch.empty((n, k), dtype=torch.float32, device=self.dev)
+        else:
+            self.ids = self.dists = None
         self.last_stats: dict = {}
 
     @property
     def slice_bounds(self) -> tuple[int, int]:
-        lo = min(self.rank * self.s, self.n)
-        return lo, min(lo + self.s, self.n)
+        return self._slice
 
-    def build(self, x_slice: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        """``x_slice``: this rank's rows ``slice_bounds`` as CUDA float32.
-        Returns (ids, dists) of shape (n, k) on every rank (valid on all)."""
-        lo, hi = self.slice_bounds
-        assert x_slice.shape == (hi - lo, self.d)
-        self._marks = []
-        self._mark("start")
-        self.flag.zero_()
-        api.pack_u8(x_slice, self.packed[lo:hi], self.norms[lo:hi], self.flag)
-        self._mark("pack")
-        if self.world > 1:
-            dist.all_reduce(self.flag, op=dist.ReduceOp.MAX, group=self.group)
-            dist.all_gather_into_tensor(self.packed, self.packed[self.rank * self.s:(self.rank + 1) * self.s],
-                                        group=self.group)
-            dist.all_gather_into_tensor(self.norms, self.norms[self.rank * self.s:(self.rank + 1) * self.s],
-                                        group=self.group)
-        self._mark("exchange_base")
-        # The flag decides the kernel family: one host read per build.
-        integer = int(self.flag.item()) == 0
-        self._mark("flag_read")
-        sh = self.shard
-        ids = self.ids[: sh.count]
-        dists = self.dists[: sh.count]
-        if integer:
-            self.last_stats = api.knn_u8(self.packed, self.norms, self.n, self.d, sh.start, sh.count, self.k,
-                                         self.metric, ids, dists, self.scratch)
-        else:
-            if self.f32_full is None:
-                self.f32_full = torch.empty((self.world * self.s, self.d), dtype=torch.float32, device=self.dev)
-            self.f32_full[lo:hi].copy_(x_slice)
-            if self.world > 1:
-                dist.all_gather_into_tensor(self.f32_full,
-                                            self.f32_full[self.rank * self.s:(self.rank + 1) * self.s],
-                                            group=self.group)
-            if self.f32_scratch is None:
-                nb = api.knn_f32_scratch_bytes(self.n, self.d, self.max_shard, self.k)
-                self.f32_scratch = torch.empty(nb, dtype=torch.uint8, device=self.dev)
-            self.last_stats = api.knn_f32(self.f32_full, self.n, self.d, sh.start, sh.count, self.k, self.metric,
-                                          ids, dists, self.f32_scratch)
-        self._mark("knn")
-        if self.world == 1:
-            return ids, dists
-        dist.all_gather_into_tensor(self.all_ids, self.ids, group=self.group)
-        dist.all_gather_into_tensor(self.all_dists, self.dists, group=self.group)
-        out = self._unpad(self.all_ids), self._unpad(self.all_dists)
-        self._mark("gather_rows")
-        return out
+    def describe(self) -> str:
+        how = "base all-gathered" if self.mode == MODE_REPLICATE else "base blocks ring-passed"
+        return f"query-shard x{self.world}, {how}, graph rows gathered to rank 0 (NCCL inside the C ABI)"
 
-    def _mark(self, name: str) -> None:
-        if self.timing:
-            ev = torch.cuda.Event(enable_timing=True)
-            ev.record()
-            self._marks.append((name, ev))
+    def build(self, x_rows: torch.Tensor, stream=None):
+        lo, hi = self._slice
+        if tuple(x_rows.shape) != (hi - lo, self.d) or x_rows.dtype != torch.float32 or not x_rows.is_contiguous():
+            raise api.InvalidArgument("ShardedBuilder.build: expected this rank's contiguous float32 rows")
+        stats = KnngGpuStats()
+        api.check(gpu_lib().knng_gpu_brute_force_sharded(
+            x_rows.data_ptr() if x_rows.numel() else None, self.n, self.d, self.k, self.metric, self.mode,
+            self.comm.handle, None if self.ids is None else self.ids.data_ptr(),
+            None if self.dists is None else self.dists.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+            api._stream_handle(stream), ctypes.byref(stats)))
+        self.last_stats = stats.as_dict()
+        return self.ids, self.dists
 
-    def phase_ms(self) -> dict:
-        """Device time of each phase of the last build (needs .timing)."""
-        torch.cuda.synchronize()
-        return {b[0]: a[1].elapsed_time(b[1]) for a, b in zip(self._marks, self._marks[1:])}
+    def last_phase_ms(self) -> dict:
+        out = (ctypes.c_float * 6)()
+        api.check(gpu_lib().knng_gpu_comm_phase_ms(self.comm.handle, out))
+        names = ("pack", "exchange_base", "search", "fp32_exchange_search", "gather_rows", "total")
+        return dict(zip(names, [float(v) for v in out]))
 
-    def _unpad(self, t: torch.Tensor) -> torch.Tensor:
-        return unpad_shards(t, self.n, self.world)
+    def time_e2e(self, x_host: torch.Tensor, steps: int, warmup: int) -> dict:
+        """Each step: pinned host rows of this rank -> device, the sharded
+        build, and on rank 0 the graph -> pinned host memory. Max over ranks."""
+        out_ids = out_d = None
+        if self.rank == 0:
+            out_ids = torch.empty((self.n, self.k), dtype=torch.int32).pin_memory()
+            out_d = torch.empty((self.n, self.k), dtype=torch.float32).pin_memory()
+
+        def step():
+            xs = x_host.to(self.dev, non_blocking=True)
+            ids, dd = self.build(xs)
+            if self.rank == 0:
+                out_ids.copy_(ids, non_blocking=True)
+                out_d.copy_(dd, non_blocking=True)
+            torch.cuda.synchronize()
+
+        for _ in range(warmup):
+            step()
+        dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            step()
+        t = torch.tensor([(time.perf_counter() - t0) / steps], device=self.dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return {"seconds_per_build": float(t.item()), "h2d_bytes_per_step": self.n * self.d * 4,
+                "d2h_bytes_per_step": self.n * self.k * 8,
+                "api": "knng_gpu_brute_force_sharded (C ABI): pinned H2D of each rank's rows, build, "
+                       "rank 0 graph D2H"}
 
 
-class RingBuilder:
-    """Sharded build that never replicates the base: the reference's ring
-    (src/dist/brute_force_mpi.cpp:71-124, one ``MPI_Sendrecv`` right/left per
-    step) over NCCL point-to-point.
+class SingleBuilder:
+    """One GPU, no collective: the device-resident C-ABI build
+    (knng_gpu_brute_force_device) with a workspace kept between builds. Same
+    interface as ShardedBuilder."""
 
-    Rank r packs its own rows (``compute_shard``) -- they are both its query
-    shard and its base block. In step s it holds block b = (r - s) mod P,
-    scores its queries against that block (global ids, self excluded by id,
-    src/dist/brute_force_mpi.cpp:80-82), merges the block's k best into its
-    running k best by (distance, id), and meanwhile already sends the block to
-    rank r+1 and receives the next one from rank r-1 (double-buffered, the
-    transfer overlaps the kernel). Blocks smaller than k contribute what they
-    have, padded with (UINT32_MAX, +inf) like the reference's sentinels
-    (src/dist/brute_force_mpi.cpp:136-139). Integer-valued data only (the u8
-    path); ``ShardedBuilder`` handles fp32 data.
-
-    ``knn_block(q_packed, q_norms, q_id0, b_packed, b_norms, b_id0, b_count,
-    k, exclude_self) -> (ids, dists)`` and ``merge(a_ids, a_d, b_ids, b_d) ->
-    (ids, dists)`` default to the GPU kernels; tests inject CPU versions.
-    """
-
-    def __init__(self, n: int, d: int, k: int, metric: int, group=None, knn_block=None, merge=None,
-                 device=None):
+    def __init__(self, n: int, d: int, k: int, metric: int):
         self.n, self.d, self.k, self.metric = n, d, k, metric
-        self.group = group
-        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
-        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
-        self.dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-        self.shard = compute_shard(n, self.world, self.rank)
-        self.max_shard = compute_shard(n, self.world, self.world - 1).count
-        self.pitch = api.padded_dim(d) if device is None or device.type == "cuda" else d
-        ms = self.max_shard
-        self.bufs = [torch.zeros((ms, self.pitch), dtype=torch.uint8, device=self.dev) for _ in range(2)]
-        self.nbufs = [torch.zeros(ms, dtype=torch.int32, device=self.dev) for _ in range(2)]
-        self.flag = torch.zeros(1, dtype=torch.int32, device=self.dev)
-        self.knn_block = knn_block or self._gpu_knn_block
-        self.merge = merge or self._gpu_merge
-        self._scratch = None
+        self.world, self.rank = 1, 0
+        self.dev = torch.device("cuda", torch.cuda.current_device())
+        self.shard = ShardBounds(0, n)
+        self.ids = torch.empty((n, k), dtype=torch.int32, device=self.dev)
+        self.dists = torch.empty((n, k), dtype=torch.float32, device=self.dev)
+        self.ws = torch.empty(api.workspace_bytes(n, d, k), dtype=torch.uint8, device=self.dev)
+        self.last_stats: dict = {}
 
-    # -- default GPU implementations
-    def _gpu_knn_block(self, q_packed, q_norms, q_id0, b_packed, b_norms, b_id0, b_count, k, exclude_self):
-        if self._scratch is None:
-            self._scratch = torch.empty(api.knn_scratch_bytes(self.max_shard), dtype=torch.uint8, device=self.dev)
-        ids = torch.empty((q_packed.shape[0], k), dtype=torch.int32, device=self.dev)
-        dists = torch.empty((q_packed.shape[0], k), dtype=torch.float32, device=self.dev)
-        api.knn_u8_sets(q_packed, q_norms, q_id0, b_packed[:b_count], b_norms[:b_count], b_id0, self.d, k,
-                        self.metric, exclude_self, ids, dists, self._scratch)
-        return ids, dists
+    @property
+    def slice_bounds(self) -> tuple[int, int]:
+        return 0, self.n
 
-    def _gpu_merge(self, a_ids, a_d, b_ids, b_d):
-        o_ids, o_d = torch.empty_like(a_ids), torch.empty_like(a_d)
-        api.merge_topk(a_ids, a_d, b_ids, b_d, o_ids, o_d)
-        return o_ids, o_d
+    def describe(self) -> str:
+        return "one GPU (knng_gpu_brute_force_device)"
 
-    def _pad(self, ids, dists):
-        k = self.k
-        if ids.shape[1] == k:
-            return ids, dists
-        pad = k - ids.shape[1]
-        pi = torch.full((ids.shape[0], pad), -1, dtype=ids.dtype, device=ids.device)  # UINT32_MAX
-        pd = torch.full((ids.shape[0], pad), float("inf"), dtype=dists.dtype, device=dists.device)
-        return torch.cat([ids, pi], 1), torch.cat([dists, pd], 1)
+    def build(self, x: torch.Tensor, stream=None):
+        _, _, self.last_stats = api.brute_force_knn_device(x, self.k, self.metric, self.ids, self.dists, self.ws,
+                                                           stream)
+        return self.ids, self.dists
 
-    def build(self, x_shard: torch.Tensor, gather: bool = True):
-        """``x_shard``: this rank's rows (``self.shard``) as float32 on the
-        device. Returns (ids, dists) of all n rows (``gather``) or of the
-        rank's own query rows."""
-        sh = self.shard
-        cur = 0
-        self.flag.zero_()
-        if self.dev.type == "cuda":
-            api.pack_u8(x_shard, self.bufs[cur][: sh.count], self.nbufs[cur][: sh.count], self.flag)
-        else:  # CPU ranks of the host-logic test: rows are already integers
-            self.bufs[cur][: sh.count, : self.d] = x_shard.to(torch.uint8)
-            self.nbufs[cur][: sh.count] = (x_shard.to(torch.int64) ** 2).sum(1).to(torch.int32)
-        if self.world > 1:
-            dist.all_reduce(self.flag, op=dist.ReduceOp.MAX, group=self.group)
-        if int(self.flag.item()) != 0:
-            raise NotImplementedError("RingBuilder: data is not integer-valued in [0, 255]; use ShardedBuilder")
-        q_packed = self.bufs[cur][: sh.count].clone()
-        q_norms = self.nbufs[cur][: sh.count].clone()
-        best_ids = best_d = None
-        right, left = (self.rank + 1) % self.world, (self.rank - 1) % self.world
-        for step in range(self.world):
-            blk = (self.rank - step) % self.world
-            bsh = compute_shard(self.n, self.world, blk)
-            reqs = []
-            if step + 1 < self.world:
-                ops = [dist.P2POp(dist.isend, self.bufs[cur], right, group=self.group),
-                       dist.P2POp(dist.irecv, self.bufs[1 - cur], left, group=self.group),
-                       dist.P2POp(dist.isend, self.nbufs[cur], right, group=self.group),
-                       dist.P2POp(dist.irecv, self.nbufs[1 - cur], left, group=self.group)]
-                reqs = dist.batch_isend_irecv(ops)
-            own = blk == self.rank
-            kb = min(self.k, bsh.count - (1 if own else 0))
-            if kb > 0:
-                ids, dists = self.knn_block(q_packed, q_norms, sh.start, self.bufs[cur], self.nbufs[cur], bsh.start,
-                                            bsh.count, kb, own)
-                ids, dists = self._pad(ids, dists)
-                best_ids, best_d = (ids, dists) if best_ids is None else self.merge(best_ids, best_d, ids, dists)
-            for r in reqs:
-                r.wait()
-            cur = 1 - cur
-        if not gather or self.world == 1:
-            return best_ids, best_d
-        return gather_shards(best_ids, self.n, self.world, self.group), gather_shards(best_d, self.n, self.world,
-                                                                                      self.group)
+    def last_phase_ms(self) -> dict:
+        s = self.last_stats
+        return {"pack": s.get("pack_ms"), "knn": s.get("knn_ms"), "tensor_kernel": s.get("tc_ms"),
+                "total": s.get("total_ms")}
+
+    def time_e2e(self, x_host: torch.Tensor, steps: int, warmup: int) -> dict:
+        """Public host API (knng_gpu_brute_force): host rows in, host graph out."""
+        xnp = x_host.numpy()
+        for _ in range(warmup):
+            api.brute_force_knn(xnp, self.k, self.metric)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            api.brute_force_knn(xnp, self.k, self.metric)
+        sec = (time.perf_counter() - t0) / steps
+        return {"seconds_per_build": sec, "h2d_bytes_per_step": self.n * self.d * 4,
+                "d2h_bytes_per_step": self.n * self.k * 8, "api": "knng_gpu_brute_force (C ABI, host buffers)"}
+
+
+def make_builder(n: int, d: int, k: int, metric: int, ring: bool = False):
+    """The builder for this process: one GPU without torch.distributed, else
+    the sharded builder (base replicated, or ring-passed with ``ring``)."""
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    if world == 1:
+        return SingleBuilder(n, d, k, metric)
+    return ShardedBuilder(n, d, k, metric, MODE_RING if ring else MODE_REPLICATE)

@@ -229,6 +229,41 @@ int oracle_brute_force_knn(const float *x, uint64_t n, uint64_t d, uint64_t k, i
     return ORACLE_OK;
 }
 
+/*
+ * Cross-set variant of the same loop body (brute_force.hpp:355-374): every
+ * query row of `q` (id q_id0 + i) against every base row of `b` (id
+ * b_id0 + r), skipping equal ids when exclude_self is set -- the reference's
+ * distributed builder scores its local queries against a remote block this
+ * way, excluding self by global index (src/dist/brute_force_mpi.cpp:76-82).
+ */
+int oracle_knn_sets(const float *q, uint64_t n_q, uint64_t q_id0, const float *b, uint64_t n_b, uint64_t b_id0,
+                    uint64_t d, uint64_t k, int metric, int exclude_self, uint32_t *out_ids, float *out_dists)
+{
+    if (n_b == 0) return ORACLE_EMPTY;
+    if (k == 0) return ORACLE_K_ZERO;
+    if (k > n_b - (exclude_self ? 1 : 0)) return ORACLE_K_TOO_LARGE;
+#pragma omp parallel
+    {
+        oracle_topk t = {NULL, 0, k};
+        t.h = (oracle_entry *)malloc(sizeof(oracle_entry) * k);
+#pragma omp for schedule(dynamic, 16)
+        for (int64_t qi = 0; qi < (int64_t)n_q; ++qi) {
+            const float *qr = q + (uint64_t)qi * d;
+            const uint64_t qid = q_id0 + (uint64_t)qi;
+            t.size = 0;
+            for (uint64_t r = 0; r < n_b; ++r) {
+                if (exclude_self && b_id0 + r == qid) continue;
+                const float dist = metric == 0 ? oracle_squared_l2(qr, b + r * d, d)
+                                               : oracle_negative_inner_product(qr, b + r * d, d);
+                topk_push(&t, (uint32_t)(b_id0 + r), dist);
+            }
+            topk_extract_sorted(&t, out_ids + (uint64_t)qi * k, out_dists + (uint64_t)qi * k);
+        }
+        free(t.h);
+    }
+    return ORACLE_OK;
+}
+
 /* ---- dataset hash (src/bench/ground_truth.cpp:45-56, 90-101) ---------- */
 
 static uint64_t fnv_update(uint64_t s, const void *bytes, uint64_t n)

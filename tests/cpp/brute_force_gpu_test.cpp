@@ -183,6 +183,31 @@ TEST(BruteForceKnnGpu, MatchesCpuOnFloatData)
     expect_identical<knng::NegativeInnerProduct>(synthetic(700, 64, 44, false), 7);
 }
 
+// Every GPU of the node from one process (knng_gpu_brute_force_multi, NCCL
+// inside the library), replicated base and ring pass: still bit-identical to
+// the reference template. Needs two GPUs; with one it checks nothing.
+TEST(BruteForceKnnGpu, MultiGpuMatchesCpu)
+{
+    const int gpus = knng_gpu_device_count();
+    if (gpus < 2) {
+        std::printf("  (one GPU: multi-GPU expectations skipped)\n");
+        return;
+    }
+    const int use = gpus < 4 ? gpus : 4;
+    const knng::Dataset ds = synthetic(3001, 128, 45, true);
+    const knng::Knng c = knng::cpu::brute_force_knn(ds, 10, knng::L2Squared{});
+    for (bool ring : {false, true}) {
+        const knng::Knng g = knng::gpu::brute_force_knn(ds, 10, knng::L2Squared{}, knng::gpu::Options{use, ring});
+        EXPECT_TRUE(g.neighbors == c.neighbors);
+        EXPECT_TRUE(std::memcmp(g.distances.data(), c.distances.data(), c.distances.size() * sizeof(float)) == 0);
+    }
+    const knng::Dataset f = synthetic(2000, 96, 46, false);
+    const knng::Knng cf = knng::cpu::brute_force_knn(f, 8, knng::NegativeInnerProduct{});
+    const knng::Knng gf = knng::gpu::brute_force_knn(f, 8, knng::NegativeInnerProduct{}, knng::gpu::Options{use, false});
+    EXPECT_TRUE(gf.neighbors == cf.neighbors);
+    EXPECT_TRUE(std::memcmp(gf.distances.data(), cf.distances.data(), cf.distances.size() * sizeof(float)) == 0);
+}
+
 int main()
 {
     for (auto& [name, fn] : Registry::get().tests) {

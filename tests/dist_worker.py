@@ -1,5 +1,6 @@
-"""torchrun worker for tests/test_gpu_multi.py: sharded build over NCCL,
-compared on rank 0 with the single-GPU build of the same dataset."""
+"""torchrun worker for tests/test_gpu_multi.py: the C-ABI sharded build
+(replicate and ring modes, NCCL inside the library), compared on rank 0 with
+the single-GPU build of the same dataset."""
 import os
 import sys
 
@@ -10,7 +11,7 @@ import torch.distributed as dist
 sys.path.insert(0, os.path.join(os.path.dirname(__file__), ".."))
 import knng_gpu_b200 as kg  # noqa: E402
 from knng_gpu_b200 import synthetic as syn  # noqa: E402
-from knng_gpu_b200.distributed import RingBuilder, ShardedBuilder  # noqa: E402
+from knng_gpu_b200.distributed import MODE_RING, ShardedBuilder  # noqa: E402
 
 
 def main():
@@ -33,9 +34,9 @@ def main():
     # ring pass of base blocks (integer data)
     for (kind, n, d, k, metric) in [(syn.KIND_SPARSE_INT, 5003, 784, 64, 1), (syn.KIND_UNIFORM_INT, 20011, 128, 10, 0)]:
         x = syn.generate(kind, 77, n, d, p_zero=0.6)
-        rb = RingBuilder(n, d, k, metric)
-        sh = rb.shard
-        ids, dists = rb.build(torch.from_numpy(x[sh.start:sh.start + sh.count]).cuda())
+        rb = ShardedBuilder(n, d, k, metric, MODE_RING)
+        lo, hi = rb.slice_bounds
+        ids, dists = rb.build(torch.from_numpy(x[lo:hi]).cuda())
         if dist.get_rank() == 0:
             g = kg.brute_force_knn(x, k, metric)
             same = np.array_equal(ids.cpu().numpy().view(np.uint32), g.neighbors.reshape(n, k)) and \

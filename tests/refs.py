@@ -36,6 +36,9 @@ def oracle() -> ctypes.CDLL:
         lib.oracle_brute_force_knn.restype = c_int
         lib.oracle_brute_force_knn.argtypes = [c_void_p, c_uint64, c_uint64, c_uint64, c_int, c_void_p, c_uint64,
                                                c_void_p, c_void_p]
+        lib.oracle_knn_sets.restype = c_int
+        lib.oracle_knn_sets.argtypes = [c_void_p, c_uint64, c_uint64, c_void_p, c_uint64, c_uint64, c_uint64,
+                                        c_uint64, c_int, c_int, c_void_p, c_void_p]
         lib.oracle_xorshift64_stream.argtypes = [c_uint64, c_uint64, c_void_p]
         lib.oracle_next_float01.restype = c_float
         lib.oracle_next_float01.argtypes = [c_void_p]
@@ -100,6 +103,20 @@ def oracle_knn(x: np.ndarray, k: int, metric: int = 0, queries: np.ndarray | Non
     if rc != 0:
         raise ValueError(f"oracle rc={rc}")
     return ids[:nq, :k], dists[:nq, :k]
+
+
+def oracle_knn_sets(q: np.ndarray, q_id0: int, b: np.ndarray, b_id0: int, k: int, metric: int = 0,
+                    exclude_self: bool = False):
+    """Oracle cross-set KNN (global ids); returns (ids[n_q, k], dists[n_q, k])."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    ids = np.zeros((q.shape[0], k), np.uint32)
+    dists = np.zeros((q.shape[0], k), np.float32)
+    rc = oracle().oracle_knn_sets(q.ctypes.data, q.shape[0], q_id0, b.ctypes.data, b.shape[0], b_id0, b.shape[1], k,
+                                  metric, int(exclude_self), ids.ctypes.data, dists.ctypes.data)
+    if rc != 0:
+        raise ValueError(f"oracle rc={rc}")
+    return ids, dists
 
 
 def ref_knn(x: np.ndarray, k: int, metric: int = 0):

@@ -75,7 +75,7 @@ def _ring_worker(rank, world, port, n, d, k, metric, q):
         sys.path.insert(0, os.path.dirname(__file__))
         from refs import oracle_knn
         from knng_gpu_b200 import synthetic as syn
-        from knng_gpu_b200.distributed import RingBuilder
+        from ring_reference import RingSchedule
 
         x = syn.generate(syn.KIND_UNIFORM_INT, 91, n, d)
 
@@ -102,7 +102,7 @@ def _ring_worker(rank, world, port, n, d, k, metric, q):
             return (torch.from_numpy(np.take_along_axis(ids, order, 1).astype(np.uint32).view(np.int32)),
                     torch.from_numpy(np.take_along_axis(ds, order, 1)))
 
-        rb = RingBuilder(n, d, k, metric, knn_block=knn_block, merge=merge, device=torch.device("cpu"))
+        rb = RingSchedule(n, d, k, metric, knn_block=knn_block, merge=merge, device=torch.device("cpu"))
         sh = rb.shard
         ids, dists = rb.build(torch.from_numpy(x[sh.start:sh.start + sh.count]))
         full_ids, full_d = oracle_knn(x, k, metric)

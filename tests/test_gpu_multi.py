@@ -51,3 +51,30 @@ def test_python_cli_two_gpus_equals_oracle(cuda_ok, tmp_path):
     ids, dists, _, _ = kio.read_knng(out)
     oi, od = oracle_knn(x, 9, 0)
     assert np.array_equal(ids, oi) and np.array_equal(dists, od)
+
+
+@pytest.mark.parametrize("ring", [False, True])
+def test_single_process_multi_gpu_equals_oracle(cuda_ok, ring):
+    """knng_gpu_brute_force_multi (one process, NCCL inside the library) on
+    every GPU of the box: bit-identical to the oracle graph."""
+    import numpy as np
+    import torch
+
+    import knng_gpu_b200 as kg
+    from knng_gpu_b200 import synthetic as syn
+    from refs import oracle_knn
+
+    g = torch.cuda.device_count()
+    if g < 2:
+        pytest.skip("needs 2 GPUs")
+    for kind, n, d, k, metric in [(syn.KIND_UNIFORM_INT, 6007, 128, 10, 0), (syn.KIND_SPARSE_INT, 3001, 784, 64, 1)]:
+        x = syn.generate(kind, 41, n, d, p_zero=0.6)
+        out = kg.brute_force_knn_multi(x, k, metric, num_gpus=g, ring=ring)
+        oi, od = oracle_knn(x, k, metric)
+        assert np.array_equal(out.neighbors.reshape(n, k), oi)
+        assert np.array_equal(out.distances.reshape(n, k).view(np.uint32), od.view(np.uint32))
+    if not ring:
+        y = syn.generate(syn.KIND_GAUSSIAN_MIXTURE, 42, 4000, 64, components=10, sigma=0.1)
+        out = kg.brute_force_knn_multi(y, 7, 0, num_gpus=g)
+        oi, od = oracle_knn(y, 7, 0)
+        assert np.array_equal(out.neighbors.reshape(-1, 7), oi) and np.array_equal(out.distances.reshape(-1, 7), od)

@@ -142,23 +142,42 @@ def test_config3_subset_against_oracle(cuda_ok):
     assert np.array_equal(dists[q.astype(np.int64)], od)
 
 
-@pytest.mark.parametrize("metric", [0, 1])
-def test_tail_split_against_oracle_and_single_pass(cuda_ok, metric, monkeypatch):
-    """n = 40,000 rows give one full wave of 256-row query tiles on 148 SMs
-    plus a 9-tile tail, which is searched as 8 concurrent base ranges and
-    merged. Every row must equal the unsplit search, and rows from both the
-    main range and the tail must equal the oracle."""
-    n, d, k = 40_000, 128, 10
+@pytest.mark.parametrize("metric,k,d", [(0, 10, 128), (1, 10, 128), (0, 32, 200), (1, 64, 784)])
+def test_pair_kernel_matches_single_cta_kernel_and_oracle(cuda_ok, metric, k, d):
+    """The CTA-pair kernel splits the (query tile, base tile) space into equal
+    ranges, so most 256-row query tiles are cut between two pairs and merged
+    afterwards. Every row must equal the single-CTA kernel (which the
+    allocation-free entry point runs), and seeded rows the oracle."""
+    import torch
+
+    from knng_gpu_b200 import _native, api
+
+    n = 40_000 if d <= 256 else 12_000
     kind = syn.KIND_UNIFORM_INT if metric == 0 else syn.KIND_SPARSE_INT
-    x = syn.generate(kind, 77, n, d, p_zero=0.6)
-    ids, dists, _ = run_gpu(x, k, metric)
-    monkeypatch.setenv("KNNG_GPU_TAIL_SPLIT", "0")
-    ids1, dists1, _ = run_gpu(x, k, metric)
-    assert np.array_equal(ids, ids1) and np.array_equal(dists, dists1)
-    q = np.concatenate([syn.sample_ids(5, 37_888, 32), 37_888 + syn.sample_ids(6, n - 37_888, 32)])
+    x = syn.generate(kind, 77 + k, n, d, p_zero=0.6)
+    dev = torch.device("cuda", 0)
+    xt = torch.from_numpy(x).to(dev)
+    packed = torch.empty((n, api.padded_dim(d)), dtype=torch.uint8, device=dev)
+    norms = torch.empty(n, dtype=torch.int32, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    api.pack_u8(xt, packed, norms, flag)
+    ids = torch.empty((n, k), dtype=torch.int32, device=dev)
+    dists = torch.empty((n, k), dtype=torch.float32, device=dev)
+    scratch = torch.empty(api.knn_scratch_bytes(n, k), dtype=torch.uint8, device=dev)
+    api.knn_u8(packed, norms, n, d, 0, n, k, metric, ids, dists, scratch)
+    ids1 = torch.empty_like(ids)
+    dists1 = torch.empty_like(dists)
+    st = _native.gpu_lib().knng_gpu_knn_u8_noalloc(packed.data_ptr(), norms.data_ptr(), n, d, 0, n, k, metric,
+                                                   ids1.data_ptr(), dists1.data_ptr(), None, None)
+    api.check(st)
+    torch.cuda.synchronize()
+    assert torch.equal(ids, ids1) and torch.equal(dists.view(torch.int32), dists1.view(torch.int32))
+    q = np.concatenate([syn.sample_ids(5, n, 48), np.array([0, 255, 256, n - 1], np.uint64)])
     oi, od = oracle_knn(x, k, metric, queries=q)
-    assert np.array_equal(ids[q.astype(np.int64)], oi)
-    assert np.array_equal(dists[q.astype(np.int64)], od)
+    gi = ids.cpu().numpy().view(np.uint32)
+    gd = dists.cpu().numpy()
+    assert np.array_equal(gi[q.astype(np.int64)], oi)
+    assert np.array_equal(gd[q.astype(np.int64)], od)
 
 
 @pytest.mark.parametrize("metric", [0, 1])

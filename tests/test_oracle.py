@@ -124,3 +124,20 @@ def test_recall_at_k():
     truth = np.array([[1, 2, 3], [0, 2, 3]], np.uint32)
     approx = np.array([[1, 1, 9], [0, 2, 3]], np.uint32)
     assert abs(lib.oracle_recall_at_k(approx.ctypes.data, truth.ctypes.data, 2, 3) - 4 / 6) < 1e-12
+
+
+def test_cross_set_oracle_equals_reference_subset_loop():
+    """oracle_knn_sets with self exclusion equals the reference's own loop
+    body run for the same query rows (ref_subset_knn)."""
+    from refs import oracle_knn_sets, ref_subset_knn, reference
+
+    if reference() is None:
+        pytest.skip("oracle/_ref not built")
+    from knng_gpu_b200 import synthetic as syn
+
+    x = syn.generate(syn.KIND_GAUSSIAN_MIXTURE, 7, 900, 24, components=5, sigma=0.2)
+    q = np.arange(100, 250, dtype=np.uint64)
+    for metric in (0, 1):
+        oi, od = oracle_knn_sets(x[100:250], 100, x, 0, 9, metric, True)
+        ri, rd = ref_subset_knn(x, 9, metric, q)
+        assert np.array_equal(oi, ri) and np.array_equal(od.view(np.uint32), rd.view(np.uint32))

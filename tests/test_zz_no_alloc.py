@@ -62,14 +62,20 @@ def test_noalloc_matches_regular_entry_twice(cuda_ok, metric, k, n, d, seed):
     q_begin, q_count = 7, n - 19
     ref_ids = torch.empty((q_count, k), dtype=torch.int32, device=dev)
     ref_d = torch.empty((q_count, k), dtype=torch.float32, device=dev)
-    scratch = torch.empty(api.knn_scratch_bytes(q_count), dtype=torch.uint8, device=dev)
+    scratch = torch.empty(api.knn_scratch_bytes(q_count, k), dtype=torch.uint8, device=dev)
     ref_stats = api.knn_u8(packed, norms, n, d, q_begin, q_count, k, metric, ref_ids, ref_d, scratch)
 
-    for _ in range(2):
+    for call in range(2):
         ids = torch.full((q_count, k), -1, dtype=torch.int32, device=dev)
         dists = torch.full((q_count, k), -1.0, dtype=torch.float32, device=dev)
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info(dev)[0]
         stats = _noalloc(packed, norms, n, d, q_begin, q_count, k, metric, ids, dists, stream)
         torch.cuda.synchronize()
+        if call == 1:
+            # The point of the entry point: once the library is loaded and the
+            # array's address resolved, a call takes no device memory.
+            assert torch.cuda.mem_get_info(dev)[0] == free_before
         assert torch.equal(ids, ref_ids)
         assert torch.equal(dists.view(torch.int32), ref_d.view(torch.int32))
         assert stats.fallback_rows == ref_stats["fallback_rows"]
