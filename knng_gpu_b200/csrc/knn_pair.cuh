@@ -34,11 +34,15 @@
 #include <cstdint>
 
 #include "knn_tc.cuh"
+#include "schedule.cuh"
 
 namespace knng_b200 {
 
 constexpr int kPairTile = 256;    // base rows per tile, query rows per pair
-constexpr int kPairThreads = 64 + 128;
+// Threads of a pair CTA with EPI epilogue warps (4: one per TMEM lane
+// quarter, each over all 256 columns of a tile; 8 or 16: two or four per
+// quarter, each over a 128- or 64-column slice).
+constexpr int pair_threads(int epi) { return 64 + 32 * epi; }
 constexpr int kPairNormSlots = 8;  // key-offset slots (one base tile each)
 
 struct PairParams {
@@ -54,10 +58,7 @@ struct PairParams {
     uint32_t k;
     uint32_t kchunks;
     uint32_t stages;
-    uint32_t n_qtiles;   // ceil(n_queries / 256)
-    uint32_t n_btiles;   // ceil(n_base / 256)
-    uint32_t n_pairs;    // CTA pairs in the grid
-    uint64_t total;      // n_qtiles * n_btiles
+    TileSchedule sched;  // units = CTA pairs; 256-row query tiles, 256-row base tiles
     uint32_t* out_ids;
     float* out_dists;
     int32_t* part_keys;  // [2 * n_pairs][256][k] partial lists of cut query tiles
@@ -66,22 +67,28 @@ struct PairParams {
     uint32_t* fallback_count;
     int* error;
     const int* skip_flag;  // optional: non-zero -> the data is not integer-valued, do nothing
+    const int32_t* seed_in;  // optional: per query row, an upper bound on its k-th key
+    int32_t* seed_out;       // seeding pass: write each query row's k-th key instead of its list
     long long wait_limit;  // clock cycles before a wait gives up
     uint32_t test_mode;    // 1: the leader's producer withholds one arrival (timeout test)
-    uint32_t debug_flags;  // profiling builds only: 1 no filtering, 2 no TMEM loads, 4 no MMAs
+    uint32_t debug_flags;  // profiling builds only: 1 no filtering, 2 no TMEM loads, 4 no MMAs, 512 clocks
+    unsigned long long* debug_clocks;  // profiling builds only (flag 512): per-role cycle counters
 };
 
-// First work item of pair p (stream-K split of [0, total)).
-__host__ __device__ inline uint64_t pair_work_begin(uint64_t total, uint32_t n_pairs, uint32_t p)
-{
-    return total * p / n_pairs;
-}
+#ifdef KNNG_GPU_EXPERIMENTS
+constexpr bool kPairProfile = true;
+#else
+constexpr bool kPairProfile = false;
+#endif
 
 struct SmemLayoutPair {
-    uint32_t a_off, aug_off, b_off, norm_off, slow_off, bar_off, total, stage_bytes;
+    uint32_t a_off, aug_off, b_off, norm_off, merge_off, bar_off, total, stage_bytes;
 };
 
-__host__ __device__ inline SmemLayoutPair smem_layout_pair(uint32_t kchunks, uint32_t stages, bool l2)
+// merge_kcap > 0: two slots of 128 rows x merge_kcap (key, id) pairs where
+// the column slices' lists of a row meet at the end of a segment.
+__host__ __device__ inline SmemLayoutPair smem_layout_pair(uint32_t kchunks, uint32_t stages, bool l2,
+                                                           uint32_t merge_kcap = 0)
 {
     SmemLayoutPair L;
     L.stage_bytes = kBoxBytes + (l2 ? kAugBox : 0);
@@ -89,8 +96,8 @@ __host__ __device__ inline SmemLayoutPair smem_layout_pair(uint32_t kchunks, uin
     L.aug_off = kchunks * kBoxBytes;
     L.b_off = L.aug_off + (l2 ? kAugBox : 0);
     L.norm_off = L.b_off + stages * L.stage_bytes;
-    L.slow_off = L.norm_off + (l2 ? kPairNormSlots * kPairTile * 4 : 0);
-    L.bar_off = L.slow_off + 128 * kSlowPitch * 4;
+    L.merge_off = L.norm_off + (l2 ? kPairNormSlots * kPairTile * 4 : 0);
+    L.bar_off = L.merge_off + 2 * kTileRows * merge_kcap * 8;
     L.total = L.bar_off + 512;
     return L;
 }
@@ -98,25 +105,30 @@ __host__ __device__ inline SmemLayoutPair smem_layout_pair(uint32_t kchunks, uin
 // UMMA instruction descriptor of the pair tile (M = 256 over two CTAs).
 __host__ __device__ constexpr uint32_t idesc_pair_u8() { return idesc_u8_s32(2 * kTileRows, kPairTile); }
 
-template <int METRIC, class TopK>
-__global__ void __launch_bounds__(kPairThreads, 1) knn_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
+template <int METRIC, class TopK, int EPI>
+__global__ void __launch_bounds__(pair_threads(EPI), 1) knn_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
                                                                    const __grid_constant__ CUtensorMap tmap_b,
                                                                    const __grid_constant__ CUtensorMap tmap_baug,
                                                                    const __grid_constant__ CUtensorMap tmap_norm,
                                                                    const PairParams p)
 {
     constexpr bool kL2 = METRIC == 0;
-    // Loads of the next 64 columns overlap the filter of the current ones
-    // when the register list is small.
-    constexpr bool kPipe = TopK::kRegs <= 32;
+    static_assert(EPI == 4 || EPI == 8 || EPI == 16, "epilogue warps");
+    constexpr int kSlices = EPI / 4;             // column slices per tile
+    constexpr int kSliceCols = kPairTile / kSlices;
+    constexpr int kSteps = kSliceCols / 32;      // 32-column steps per tile and warp
+    constexpr int kMergeCap = kSlices > 1 ? TopK::kRegs / 2 : 0;
+    // With four epilogue warps the load of the next 32 columns overlaps the
+    // filter of the current ones (when the register list is small).
+    constexpr bool kPipe = EPI == 4 && TopK::kRegs <= 32;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const SmemLayoutPair L = smem_layout_pair(p.kchunks, p.stages, kL2);
+    const SmemLayoutPair L = smem_layout_pair(p.kchunks, p.stages, kL2, kMergeCap);
     uint8_t* sA = smem + L.a_off;
     uint8_t* sAaug = smem + L.aug_off;
     uint8_t* sB = smem + L.b_off;
     int32_t* sNorm = reinterpret_cast<int32_t*>(smem + L.norm_off);
-    int32_t* sSlow = reinterpret_cast<int32_t*>(smem + L.slow_off);
+    int32_t* sMerge = reinterpret_cast<int32_t*>(smem + L.merge_off);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off);
     const uint32_t S = p.stages;
     uint64_t* full = bars;         // [S] leader: stage loaded (both CTAs' bytes)
@@ -124,14 +136,17 @@ __global__ void __launch_bounds__(kPairThreads, 1) knn_pair_kernel(const __grid_
     uint64_t* a_full = bars + 32;  // leader: query rows loaded
     uint64_t* a_empty = bars + 33; // both: MMAs of a query tile done
     uint64_t* tfull = bars + 34;   // [2] both: accumulator buffer ready
-    uint64_t* tempty = bars + 36;  // [2] leader: buffer drained by all 8 epilogue warps
+    uint64_t* tempty = bars + 36;  // [2] leader: buffer drained by the epilogue warps of both CTAs
     uint64_t* nfull = bars + 38;   // [8] local: key offsets of a tile landed
-    uint64_t* nempty = bars + 46;  // [8] local: key offsets read by the 4 epilogue warps
+    uint64_t* nempty = bars + 46;  // [8] local: key offsets read by the epilogue warps
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 54);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 55);
     // Base tiles whose MMAs are complete (published by one epilogue thread
     // after its hand-off wait): a B stage is reused once its tile is counted.
     volatile uint32_t* tiles_done = reinterpret_cast<volatile uint32_t*>(bars + 56);
+    // Per lane quarter: arrivals of its slice warps at the segment-end merge
+    // (a bounded counter barrier, so an aborting warp cannot strand the others).
+    uint32_t* merge_cnt = reinterpret_cast<uint32_t*>(bars + 57);
     const bool stage_commits = S < 2 * p.kchunks;
     const uint32_t stage_bytes = L.stage_bytes;
     const long long lim_cycles = p.wait_limit;
@@ -145,9 +160,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) knn_pair_kernel(const __grid_
     const bool leader = cta == 0;
     const uint32_t leader_rank = crank & ~1u;
     const uint32_t pair = blockIdx.x >> 1;
-    const uint64_t w0 = pair_work_begin(p.total, p.n_pairs, pair);
-    const uint64_t w1 = pair_work_begin(p.total, p.n_pairs, pair + 1);
-    const uint32_t nbt = p.n_btiles;
+    const uint32_t nbt = p.sched.n_btiles;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S; ++s) {
@@ -158,14 +171,15 @@ __global__ void __launch_bounds__(kPairThreads, 1) knn_pair_kernel(const __grid_
         mbar_init(a_empty, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 8);
+            mbar_init(&tempty[b], 2 * EPI);
         }
         for (int s = 0; s < kPairNormSlots; ++s) {
             mbar_init(&nfull[s], 1);
-            mbar_init(&nempty[s], 4);
+            mbar_init(&nempty[s], EPI);
         }
         *abort_flag = 0;
         *tiles_done = 0;
+        for (int q = 0; q < 4; ++q) merge_cnt[q] = 0;
         fence_barrier_init();
         prefetch_tensormap(&tmap_q);
         prefetch_tensormap(&tmap_b);
@@ -202,61 +216,57 @@ __global__ void __launch_bounds__(kPairThreads, 1) knn_pair_kernel(const __grid_
             for (int i = 0; i < 16; ++i) last_use[i] = 0;
             uint64_t load_idx = 0;
             bool ok = true, withheld = false;
-            uint32_t qt = static_cast<uint32_t>(w0 / nbt), bt = static_cast<uint32_t>(w0 % nbt);
             uint32_t acc_i = 0;
-            for (uint64_t w = w0; w < w1 && ok; ++w, ++acc_i) {
-                if (w == w0 || bt == 0) {
-                    ok = mbar_wait(a_empty, a_par ^ 1, abort_flag, lim_cycles);
-                    if (!ok) break;
-                    a_par ^= 1;
-                    if (leader) mbar_arrive_expect_tx(a_full, 2 * p.kchunks * kBoxBytes);
-                    for (uint32_t kc = 0; kc < p.kchunks; ++kc)
-                        tma_load_2d_pair(sA + kc * kBoxBytes, &tmap_q, kc * kChunkBytes,
-                                         qt * kPairTile + cta * kTileRows, a_full_l);
-                }
-                if constexpr (kL2) {
-                    const uint32_t slot = acc_i % kPairNormSlots;
-                    if (acc_i >= kPairNormSlots) {
-                        ok = mbar_wait(&nempty[slot], (acc_i / kPairNormSlots - 1) & 1, abort_flag, lim_cycles);
-                        if (!ok) break;
+            uint32_t qt, b0, b1, pslot;
+            for (uint32_t sg = 0; ok && schedule_segment(p.sched, pair, sg, qt, b0, b1, pslot); ++sg) {
+                ok = mbar_wait(a_empty, a_par ^ 1, abort_flag, lim_cycles);
+                if (!ok) break;
+                a_par ^= 1;
+                if (leader) mbar_arrive_expect_tx(a_full, 2 * p.kchunks * kBoxBytes);
+                for (uint32_t kc = 0; kc < p.kchunks; ++kc)
+                    tma_load_2d_pair(sA + kc * kBoxBytes, &tmap_q, kc * kChunkBytes, qt * kPairTile + cta * kTileRows,
+                                     a_full_l);
+                for (uint32_t bt = b0; bt < b1 && ok; ++bt, ++acc_i) {
+                    if constexpr (kL2) {
+                        const uint32_t slot = acc_i % kPairNormSlots;
+                        if (acc_i >= kPairNormSlots) {
+                            ok = mbar_wait(&nempty[slot], (acc_i / kPairNormSlots - 1) & 1, abort_flag, lim_cycles);
+                            if (!ok) break;
+                        }
+                        mbar_arrive_expect_tx(&nfull[slot], kPairTile * 4);
+                        tma_load_1d(sNorm + slot * kPairTile, &tmap_norm, bt * kPairTile, &nfull[slot]);
                     }
-                    mbar_arrive_expect_tx(&nfull[slot], kPairTile * 4);
-                    tma_load_1d(sNorm + slot * kPairTile, &tmap_norm, bt * kPairTile, &nfull[slot]);
-                }
-                for (uint32_t kc = 0; kc < p.kchunks; ++kc) {
-                    if (stage_commits) {
-                        ok = mbar_wait(&empty[stage], phase ^ 1, abort_flag, lim_cycles);
-                        if (!ok) break;
-                    } else if (load_idx >= S) {
-                        ok = spin_until_geq(tiles_done, rel_tile + 1, abort_flag, 128, lim_cycles);
-                        if (!ok) break;
-                        if (++rel_kc == p.kchunks) {
-                            rel_kc = 0;
-                            ++rel_tile;
+                    for (uint32_t kc = 0; kc < p.kchunks; ++kc) {
+                        if (stage_commits) {
+                            ok = mbar_wait(&empty[stage], phase ^ 1, abort_flag, lim_cycles);
+                            if (!ok) break;
+                        } else if (load_idx >= S) {
+                            ok = spin_until_geq(tiles_done, rel_tile + 1, abort_flag, 128, lim_cycles);
+                            if (!ok) break;
+                            if (++rel_kc == p.kchunks) {
+                                rel_kc = 0;
+                                ++rel_tile;
+                            }
+                        }
+                        ++load_idx;
+                        const bool aug_here = kL2 && kc + 1 == p.kchunks;
+                        const uint32_t bytes = 2 * (kBoxBytes + (aug_here ? kAugBox : 0));
+                        // Timeout test: the leader withholds the arrival of one
+                        // stage, so its phase never completes.
+                        const bool skip = p.test_mode == 1 && leader && !withheld;
+                        if (skip) withheld = true;
+                        if (leader && !skip) mbar_arrive_expect_tx(&full[stage], bytes);
+                        uint8_t* dst = sB + stage * stage_bytes;
+                        const uint32_t bar = full0 + stage * 8;
+                        tma_load_2d_pair(dst, &tmap_b, kc * kChunkBytes, bt * kPairTile + cta * kTileRows, bar);
+                        if (aug_here)
+                            tma_load_2d_pair(dst + kBoxBytes, &tmap_baug, 0, bt * kPairTile + cta * kTileRows, bar);
+                        last_use[stage] = phase + 1;  // completes phase `phase`
+                        if (++stage == S) {
+                            stage = 0;
+                            phase ^= 1;
                         }
                     }
-                    ++load_idx;
-                    const bool aug_here = kL2 && kc + 1 == p.kchunks;
-                    const uint32_t bytes = 2 * (kBoxBytes + (aug_here ? kAugBox : 0));
-                    // Timeout test: the leader withholds the arrival of one
-                    // stage, so its phase never completes.
-                    const bool skip = p.test_mode == 1 && leader && !withheld;
-                    if (skip) withheld = true;
-                    if (leader && !skip) mbar_arrive_expect_tx(&full[stage], bytes);
-                    uint8_t* dst = sB + stage * stage_bytes;
-                    const uint32_t bar = full0 + stage * 8;
-                    tma_load_2d_pair(dst, &tmap_b, kc * kChunkBytes, bt * kPairTile + cta * kTileRows, bar);
-                    if (aug_here) tma_load_2d_pair(dst + kBoxBytes, &tmap_baug, 0, bt * kPairTile + cta * kTileRows, bar);
-                    last_use[stage] = phase + 1;  // completes phase `phase`
-                    if (++stage == S) {
-                        stage = 0;
-                        phase ^= 1;
-                    }
-                }
-                if (!ok) break;
-                if (++bt == nbt) {
-                    bt = 0;
-                    ++qt;
                 }
             }
             if (!ok) abort_pair(1);
@@ -279,309 +289,316 @@ __global__ void __launch_bounds__(kPairThreads, 1) knn_pair_kernel(const __grid_
             const uint64_t stage_step = stage_bytes >> 4;
             uint32_t s = 0, ph = 0, a_par = 0, acc_i = 0;
             bool ok = true;
-            uint32_t bt = static_cast<uint32_t>(w0 % nbt);
-            for (uint64_t w = w0; w < w1 && ok; ++w, ++acc_i) {
-                if (w == w0 || bt == 0) {
-                    ok = mbar_wait_sleep(a_full, a_par, abort_flag, lim_cycles);
-                    if (!ok) break;
-                    a_par ^= 1;
-                    tc_fence_after();
-                }
-                const uint32_t buf = acc_i & 1u;
-                ok = mbar_wait_sleep(&tempty[buf], ((acc_i >> 1) & 1u) ^ 1u, abort_flag, lim_cycles);
+            const bool prof = kPairProfile && (p.debug_flags & 512u) && p.debug_clocks;
+            long long c_te = 0, c_fu = 0, c_t0 = clock64();
+            uint32_t qt, b0, b1, pslot;
+            for (uint32_t sg = 0; ok && schedule_segment(p.sched, pair, sg, qt, b0, b1, pslot); ++sg) {
+                ok = mbar_wait_sleep(a_full, a_par, abort_flag, lim_cycles);
                 if (!ok) break;
+                a_par ^= 1;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + buf * kPairTile;
-                for (uint32_t kc = 0; kc < p.kchunks; ++kc) {
-                    ok = mbar_wait_sleep(&full[s], ph, abort_flag, lim_cycles);
+                for (uint32_t bt = b0; bt < b1; ++bt, ++acc_i) {
+                    const uint32_t buf = acc_i & 1u;
+                    const long long w_te = prof ? clock64() : 0;
+                    // profiling flag 8: plain try_wait polling instead of the suspend hint
+                    ok = (kPairProfile && (p.debug_flags & 8u))
+                             ? mbar_wait(&tempty[buf], ((acc_i >> 1) & 1u) ^ 1u, abort_flag, lim_cycles)
+                             : mbar_wait_sleep(&tempty[buf], ((acc_i >> 1) & 1u) ^ 1u, abort_flag, lim_cycles);
+                    if (prof) c_te += clock64() - w_te;
                     if (!ok) break;
                     tc_fence_after();
-                    const uint64_t ad = a_desc0 + kc * kBoxStep;
-                    const uint64_t bd = b_desc0 + s * stage_step;
-                    if (!(p.debug_flags & 4u)) {
+                    const uint32_t d_tmem = tmem_base + buf * kPairTile;
+                    for (uint32_t kc = 0; kc < p.kchunks; ++kc) {
+                        const long long w_fu = prof ? clock64() : 0;
+                        ok = (kPairProfile && (p.debug_flags & 8u)) ? mbar_wait(&full[s], ph, abort_flag, lim_cycles)
+                                                                    : mbar_wait_sleep(&full[s], ph, abort_flag, lim_cycles);
+                        if (prof) c_fu += clock64() - w_fu;
+                        if (!ok) break;
+                        tc_fence_after();
+                        const uint64_t ad = a_desc0 + kc * kBoxStep;
+                        const uint64_t bd = b_desc0 + s * stage_step;
+                        if (!(p.debug_flags & 4u)) {
 #pragma unroll
-                        for (int ks = 0; ks < kChunkBytes / 32; ++ks)
-                            umma_u8_pair(d_tmem, ad + 2 * ks, bd + 2 * ks, idesc, (kc > 0 || ks > 0) ? 1u : 0u);
-                        if constexpr (kL2) {
-                            if (kc + 1 == p.kchunks)
-                                umma_u8_pair(d_tmem, a_aug_desc, b_aug_desc0 + s * stage_step, idesc, 1u);
+                            for (int ks = 0; ks < kChunkBytes / 32; ++ks)
+                                umma_u8_pair(d_tmem, ad + 2 * ks, bd + 2 * ks, idesc, (kc > 0 || ks > 0) ? 1u : 0u);
+                            if constexpr (kL2) {
+                                if (kc + 1 == p.kchunks && !(kPairProfile && (p.debug_flags & 1024u)))
+                                    umma_u8_pair(d_tmem, a_aug_desc, b_aug_desc0 + s * stage_step, idesc, 1u);
+                            }
+                        }
+                        if (stage_commits) umma_commit_pair(&empty[s]);
+                        if (++s == S) {
+                            s = 0;
+                            ph ^= 1;
                         }
                     }
-                    if (stage_commits) umma_commit_pair(&empty[s]);
-                    if (++s == S) {
-                        s = 0;
-                        ph ^= 1;
-                    }
+                    if (!ok) break;
+                    umma_commit_pair(&tfull[buf]);
                 }
-                if (!ok) break;
-                umma_commit_pair(&tfull[buf]);
-                const bool qtile_ends = bt + 1 == nbt || w + 1 == w1;
-                if (qtile_ends) umma_commit_pair(a_empty);
-                if (++bt == nbt) bt = 0;
+                // The query tile's MMAs are issued: its A buffer frees when they complete.
+                if (ok) umma_commit_pair(a_empty);
+            }
+            if (prof) {
+                atomicAdd(p.debug_clocks + 4, static_cast<unsigned long long>(c_te));
+                atomicAdd(p.debug_clocks + 5, static_cast<unsigned long long>(c_fu));
+                atomicAdd(p.debug_clocks + 6, static_cast<unsigned long long>(clock64() - c_t0));
             }
             if (!ok) abort_pair(2);
         }
     } else {
-        // ------------------------------------------------ epilogue (4 warps per CTA)
+        // ------------------------------------------------ epilogue (EPI warps per CTA)
+        // Warp -> TMEM lane quarter (hardware rule: warp w reads lanes
+        // 32 (w % 4) ..) and column slice; thread <-> one query row.
         const int quarter = warp & 3;
+        const int slice = (warp - 2) >> 2;
         const uint32_t row = quarter * 32 + lane;
-        int32_t* slow = sSlow + row * kSlowPitch;
+        const int cbase = slice * kSliceCols;  // first column of this warp's slice
         const uint32_t tempty_l = mapa_shared(smem_u32(tempty), leader_rank);
-        uint32_t qt = static_cast<uint32_t>(w0 / nbt), bt = static_cast<uint32_t>(w0 % nbt);
         uint32_t acc_i = 0;
         bool ok = true;
-        uint64_t w = w0;
-        while (w < w1 && ok) {
-            const uint64_t seg_lo = w;
-            const uint64_t q_end = static_cast<uint64_t>(qt + 1) * nbt;
-            const uint64_t seg_hi = q_end < w1 ? q_end : w1;
-            const bool complete = bt == 0 && seg_hi == q_end;
+        const bool prof = kPairProfile && (p.debug_flags & 512u) && p.debug_clocks && lane == 0;
+        long long c_tf = 0, c_slow = 0, c_t0 = clock64();
+        unsigned long long n_slow = 0, n_slow_calls = 0;
+        uint32_t merge_round = 0;  // target of this warp's next merge barrier
+        uint32_t qt, b0, b1, pslot;
+        for (uint32_t sg = 0; ok && schedule_segment(p.sched, pair, sg, qt, b0, b1, pslot); ++sg) {
+            const bool complete = b0 == 0 && b1 == nbt;
             const uint32_t qlocal = qt * kPairTile + cta * kTileRows + row;
             const bool qvalid = qlocal < p.n_queries;
             const uint32_t self_id = p.exclude_self ? p.query_id0 + qlocal : UINT32_MAX;
-            int32_t qnorm = 0;
-            if constexpr (kL2) {
-                if (qvalid && complete) {
-                    const uint4* a4 = reinterpret_cast<const uint4*>(p.query_packed + static_cast<uint64_t>(qlocal) * p.pitch +
-                                                                     p.data_bytes);
-                    const uint4 x0 = a4[0], x1 = a4[1];
-                    uint32_t sb = 0;
-                    sb = __dp4a(x0.x, 0x01010101u, sb);
-                    sb = __dp4a(x0.y, 0x01010101u, sb);
-                    sb = __dp4a(x0.z, 0x01010101u, sb);
-                    sb = __dp4a(x0.w, 0x01010101u, sb);
-                    sb = __dp4a(x1.x, 0x01010101u, sb);
-                    sb = __dp4a(x1.y, 0x01010101u, sb);
-                    sb = __dp4a(x1.z, 0x01010101u, sb);
-                    sb = __dp4a(x1.w, 0x01010101u, sb);
-                    qnorm = p.query_norms[qlocal] - 510 * static_cast<int32_t>(sb);
-                }
-            }
             TopK tk;
             tk.init(p.k);
-            int32_t thr = tk.thr();
-            for (; w < seg_hi; ++w, ++acc_i, ++bt) {
+            // A seeded upper bound on the row's k-th key (from a pass over a
+            // sample of the base) admits only keys <= seed from the start.
+            int32_t seed_thr = INT_MAX;
+            if (p.seed_in && qvalid) {
+                const int32_t sd = p.seed_in[qlocal];
+                seed_thr = sd < INT_MAX ? sd + 1 : INT_MAX;
+            }
+            int32_t thr = min(tk.thr(), seed_thr);
+            for (uint32_t bt = b0; bt < b1; ++bt, ++acc_i) {
                 const uint32_t buf = acc_i & 1u;
+                const long long w_tf = prof ? clock64() : 0;
                 ok = mbar_wait(&tfull[buf], (acc_i >> 1) & 1u, abort_flag, lim_cycles);
+                if (prof) c_tf += clock64() - w_tf;
                 if (!ok) break;
                 tc_fence_after();
                 if (warp == 2 && lane == 0) *tiles_done = acc_i + 1;
                 const uint32_t slot = acc_i % kPairNormSlots;
                 const int32_t* nb = sNorm + slot * kPairTile;
+                const uint64_t tile0 = static_cast<uint64_t>(bt) * kPairTile;
+                const uint32_t nvalid =
+                    p.n_base - tile0 < kPairTile ? static_cast<uint32_t>(p.n_base - tile0) : kPairTile;
+                const uint32_t col0 = p.base_id0 + static_cast<uint32_t>(tile0);
+                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * kPairTile;
+                // A column can hold a key < thr only if its accumulator
+                // exceeds lim: L2 keys are keyoff - 2 acc >= hmin - 2 acc,
+                // with hmin the smallest key offset of the column's 128-row
+                // half of the tile (the augmentation bytes are chosen per
+                // 128-row pack tile, so offsets are near-uniform within a
+                // half but not across halves); inner-product keys are -acc.
+                int32_t hmin_lo = 0, hmin_hi = 0;
                 if constexpr (kL2) {
                     ok = mbar_wait(&nfull[slot], (acc_i / kPairNormSlots) & 1u, abort_flag, lim_cycles);
                     if (!ok) break;
-                    // Smallest key offset of each 128-column half of the
-                    // tile (valid rows only; padding rows read as 0 from TMA
-                    // and are masked in the slow path). The augmentation
-                    // bytes are chosen per 128-row tile of the pack call, so
-                    // key offsets are near-uniform within a half but not
-                    // across the two halves: one bound per half keeps the
-                    // filter sharp. Lanes 0-15 hold columns 0-127.
-                    const uint64_t tile0 = static_cast<uint64_t>(bt) * kPairTile;
                     const int4 h0 = reinterpret_cast<const int4*>(nb)[2 * lane];
                     const int4 h1 = reinterpret_cast<const int4*>(nb)[2 * lane + 1];
                     const int32_t hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
                     int32_t hm = INT_MAX;
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
-                        if (tile0 + 8 * lane + e < p.n_base) hm = min(hm, hv[e]);
+                        if (8u * lane + e < nvalid) hm = min(hm, hv[e]);
 #pragma unroll
                     for (int o = 8; o > 0; o >>= 1) hm = min(hm, __shfl_xor_sync(0xffffffffu, hm, o));
-                    const int32_t hmin_lo = __shfl_sync(0xffffffffu, hm, 0);
-                    const int32_t hmin_hi = __shfl_sync(0xffffffffu, hm, 16);
-                    auto lim_of = [](int32_t h, int32_t t) -> int32_t {
+                    hmin_lo = __shfl_sync(0xffffffffu, hm, 0);
+                    hmin_hi = __shfl_sync(0xffffffffu, hm, 16);
+                }
+                auto lim_of = [](int32_t h, int32_t t) -> int32_t {
+                    if constexpr (kL2) {
                         return static_cast<int32_t>((static_cast<long long>(h) - t) >> 1);  // floor
-                    };
-                    int32_t lim_lo = lim_of(hmin_lo, thr), lim_hi = lim_of(hmin_hi, thr);
-                    const uint32_t nvalid = p.n_base - tile0 < kPairTile ? static_cast<uint32_t>(p.n_base - tile0) : kPairTile;
-                    const uint32_t col0 = p.base_id0 + static_cast<uint32_t>(tile0);
-                    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * kPairTile;
-                    // 32 columns starting at c0 hold a candidate: exact keys,
-                    // then insertion in id order.
-                    auto slow_path = [&](int32_t* vc, int c0) {
+                    } else {
+                        return -t;
+                    }
+                };
+                int32_t lim_lo = lim_of(hmin_lo, thr), lim_hi = lim_of(hmin_hi, thr);
+                // 32 columns from c0 hold an accumulator above lim: scan the
+                // 8-column sub-groups in registers; for those that pass,
+                // compute exact keys and insert in id order.
+                auto slow_path = [&](const int32_t* vc, int c0) {
+                    const long long w_sl = prof ? clock64() : 0;
+                    if (prof) ++n_slow_calls;
 #pragma unroll
-                        for (int i4 = 0; i4 < 8; ++i4) {
-                            const int4 nn = reinterpret_cast<const int4*>(nb + c0)[i4];
-                            vc[4 * i4 + 0] = nn.x - 2 * vc[4 * i4 + 0];
-                            vc[4 * i4 + 1] = nn.y - 2 * vc[4 * i4 + 1];
-                            vc[4 * i4 + 2] = nn.z - 2 * vc[4 * i4 + 2];
-                            vc[4 * i4 + 3] = nn.w - 2 * vc[4 * i4 + 3];
+                    for (int g = 0; g < 4; ++g) {
+                        const int cg = c0 + 8 * g;
+                        const int32_t* a = vc + 8 * g;
+                        const int32_t lim = cg < 128 ? lim_lo : lim_hi;
+                        const int32_t m = max(__vimax3_s32(a[0], a[1], a[2]), __vimax3_s32(a[3], a[4], a[5]));
+                        if (max(m, max(a[6], a[7])) <= lim) continue;
+                        int32_t kv[8];
+                        if constexpr (kL2) {
+                            const int4 n0 = reinterpret_cast<const int4*>(nb + cg)[0];
+                            const int4 n1 = reinterpret_cast<const int4*>(nb + cg)[1];
+                            const int32_t nv[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) kv[j] = nv[j] - 2 * a[j];
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) kv[j] = -a[j];
                         }
                         uint32_t mask = 0;
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) mask |= (vc[i] < thr ? 1u : 0u) << i;
-                        if (c0 + 32 > static_cast<int>(nvalid))
-                            mask &= c0 >= static_cast<int>(nvalid) ? 0u : (0xffffffffu >> (32 - (nvalid - c0)));
-                        if (!mask) return;
-#pragma unroll
-                        for (int i4 = 0; i4 < 8; ++i4)
-                            *reinterpret_cast<int4*>(slow + 4 * i4) =
-                                make_int4(vc[4 * i4], vc[4 * i4 + 1], vc[4 * i4 + 2], vc[4 * i4 + 3]);
+                        for (int j = 0; j < 8; ++j) mask |= (kv[j] < thr ? 1u : 0u) << j;
+                        if (cg + 8 > static_cast<int>(nvalid))
+                            mask &= cg >= static_cast<int>(nvalid) ? 0u : (0xffu >> (8 - (nvalid - cg)));
+                        if (prof && mask) ++n_slow;
                         while (mask) {
-                            const int i = __ffs(mask) - 1;
+                            const int j = __ffs(mask) - 1;
                             mask &= mask - 1;
-                            const int32_t key = slow[i];
-                            const uint32_t id = col0 + c0 + i;
+                            int32_t key = kv[7];
+#pragma unroll
+                            for (int jj = 6; jj >= 0; --jj) key = j == jj ? kv[jj] : key;
+                            const uint32_t id = col0 + cg + j;
                             if (key < thr && id != self_id) {
                                 tk.insert_increasing(key, id);
-                                thr = tk.thr();
+                                thr = min(tk.thr(), seed_thr);
                             }
                         }
                         lim_lo = lim_of(hmin_lo, thr);
                         lim_hi = lim_of(hmin_hi, thr);
-                    };
-                    auto filter64 = [&](int32_t* v, int c0) {
-                        const int32_t lim = c0 < 128 ? lim_lo : lim_hi;
-                        if (tree_max<64>(v) > lim) {
-                            if (tree_max<32>(v) > lim) slow_path(v, c0);
-                            const int32_t lim2 = c0 < 128 ? lim_lo : lim_hi;
-                            if (tree_max<32>(v + 32) > lim2) slow_path(v + 32, c0 + 32);
-                        }
-                    };
-                    auto release = [&]() {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive_cluster(tempty_l + buf * 8);
-                    };
-                    if (p.debug_flags & 3u) {
-                        // profiling: hand-off (with or without the loads), no filtering
-                        if (!(p.debug_flags & 2u)) {
-                            int32_t v[64];
-#pragma unroll
-                            for (int st = 0; st < 4; ++st) {
-                                __syncwarp();
-                                tmem_ld_32cols(taddr + st * 64, v);
-                                tmem_ld_32cols(taddr + st * 64 + 32, v + 32);
-                                tmem_ld_wait_n<64>(v);
-                                if (v[0] == INT_MIN && v[63] == INT_MIN) thr = 0;  // keep the loads
-                            }
-                        }
-                        release();
-                    } else if constexpr (kPipe) {
-                        int32_t va[64], vb[64];
-                        __syncwarp();
-                        tmem_ld_32cols(taddr, va);
-                        tmem_ld_32cols(taddr + 32, va + 32);
-                        tmem_ld_wait_n<64>(va);
-                        // st 0
-                        tmem_ld_32cols(taddr + 64, vb);
-                        tmem_ld_32cols(taddr + 96, vb + 32);
-                        filter64(va, 0);
-                        __syncwarp();
-                        tmem_ld_wait_n<64>(vb);
-                        // st 1
-                        tmem_ld_32cols(taddr + 128, va);
-                        tmem_ld_32cols(taddr + 160, va + 32);
-                        filter64(vb, 64);
-                        __syncwarp();
-                        tmem_ld_wait_n<64>(va);
-                        // st 2
-                        tmem_ld_32cols(taddr + 192, vb);
-                        tmem_ld_32cols(taddr + 224, vb + 32);
-                        filter64(va, 128);
-                        __syncwarp();
-                        tmem_ld_wait_n<64>(vb);
-                        // st 3: every column is in registers
-                        release();
-                        filter64(vb, 192);
-                    } else {
-#pragma unroll
-                        for (int st = 0; st < 4; ++st) {
-                            int32_t v[64];
+                    }
+                    if (prof) c_slow += clock64() - w_sl;
+                };
+                // 32 columns from c0: one maximum against lim.
+                auto filter32 = [&](const int32_t* v, int c0) {
+                    if (tree_max<32>(v) > (c0 < 128 ? lim_lo : lim_hi)) slow_path(v, c0);
+                };
+                auto release = [&]() {
+                    tc_fence_before();
+                    __syncwarp();
+                    // Default semantics (release at CTA scope): the tcgen05
+                    // fence above orders the TMEM reads; a cluster-scope
+                    // release here would cost a membar per hand-off.
+                    if (lane == 0) mbar_arrive_remote(tempty_l + buf * 8);
+                };
+                const uint32_t tslice = taddr + cbase;
+                if (p.debug_flags & 3u) {
+                    // profiling: hand-off (with or without the loads), no filtering
+                    if (!(p.debug_flags & 2u)) {
+                        int32_t v[32];
+#pragma unroll 1
+                        for (int st = 0; st < kSteps; ++st) {
                             __syncwarp();
-                            tmem_ld_32cols(taddr + st * 64, v);
-                            tmem_ld_32cols(taddr + st * 64 + 32, v + 32);
-                            tmem_ld_wait_n<64>(v);
-                            if (st == 3) release();
-                            filter64(v, st * 64);
+                            tmem_ld_32cols(tslice + st * 32, v);
+                            tmem_ld_wait_n<32>(v);
+                            if (v[0] == INT_MIN && v[31] == INT_MIN) thr = 0;  // keep the loads
                         }
                     }
+                    release();
+                } else if constexpr (kPipe) {
+                    // The load of the next 32 columns is in flight while the
+                    // current ones are filtered; the buffer goes back as soon
+                    // as the last columns are in registers.
+                    int32_t va[32], vb[32];
+                    __syncwarp();
+                    tmem_ld_32cols(tslice, va);
+                    tmem_ld_wait_n<32>(va);
+#pragma unroll 1
+                    for (int st = 0; st < kSteps; st += 2) {
+                        __syncwarp();
+                        tmem_ld_32cols(tslice + (st + 1) * 32, vb);
+                        filter32(va, cbase + st * 32);
+                        __syncwarp();
+                        tmem_ld_wait_n<32>(vb);
+                        if (st + 2 < kSteps) {
+                            tmem_ld_32cols(tslice + (st + 2) * 32, va);
+                        } else {
+                            release();
+                        }
+                        filter32(vb, cbase + (st + 1) * 32);
+                        if (st + 2 < kSteps) {
+                            __syncwarp();
+                            tmem_ld_wait_n<32>(va);
+                        }
+                    }
+                } else {
+#pragma unroll 1
+                    for (int st = 0; st < kSteps; ++st) {
+                        int32_t v[32];
+                        __syncwarp();
+                        tmem_ld_32cols(tslice + st * 32, v);
+                        tmem_ld_wait_n<32>(v);
+                        if (st == kSteps - 1) release();
+                        filter32(v, cbase + st * 32);
+                    }
+                }
+                if constexpr (kL2) {
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&nempty[slot]);
-                } else {
-                    // Inner product: key = -acc, no offsets.
-                    int32_t lim = -thr;
-                    const uint64_t tile0 = static_cast<uint64_t>(bt) * kPairTile;
-                    const uint32_t nvalid = p.n_base - tile0 < kPairTile ? static_cast<uint32_t>(p.n_base - tile0) : kPairTile;
-                    const uint32_t col0 = p.base_id0 + static_cast<uint32_t>(tile0);
-                    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * kPairTile;
-                    auto slow_path = [&](int32_t* vc, int c0) {
-                        uint32_t mask = 0;
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            vc[i] = -vc[i];
-                            mask |= (vc[i] < thr ? 1u : 0u) << i;
-                        }
-                        if (c0 + 32 > static_cast<int>(nvalid))
-                            mask &= c0 >= static_cast<int>(nvalid) ? 0u : (0xffffffffu >> (32 - (nvalid - c0)));
-                        if (!mask) return;
-#pragma unroll
-                        for (int i4 = 0; i4 < 8; ++i4)
-                            *reinterpret_cast<int4*>(slow + 4 * i4) =
-                                make_int4(vc[4 * i4], vc[4 * i4 + 1], vc[4 * i4 + 2], vc[4 * i4 + 3]);
-                        while (mask) {
-                            const int i = __ffs(mask) - 1;
-                            mask &= mask - 1;
-                            const int32_t key = slow[i];
-                            const uint32_t id = col0 + c0 + i;
-                            if (key < thr && id != self_id) {
-                                tk.insert_increasing(key, id);
-                                thr = tk.thr();
-                            }
-                        }
-                        lim = -thr;
-                    };
-                    auto filter64 = [&](int32_t* v, int c0) {
-                        if (tree_max<64>(v) > lim) {
-                            if (tree_max<32>(v) > lim) slow_path(v, c0);
-                            if (tree_max<32>(v + 32) > lim) slow_path(v + 32, c0 + 32);
-                        }
-                    };
-                    auto release = [&]() {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive_cluster(tempty_l + buf * 8);
-                    };
-#pragma unroll
-                    for (int st = 0; st < 4; ++st) {
-                        int32_t v[64];
-                        __syncwarp();
-                        tmem_ld_32cols(taddr + st * 64, v);
-                        tmem_ld_32cols(taddr + st * 64 + 32, v + 32);
-                        tmem_ld_wait_n<64>(v);
-                        if (st == 3) release();
-                        filter64(v, st * 64);
-                    }
                 }
             }
             if (!ok) break;
-            // Segment done: final graph rows, or a partial list of a query
-            // tile cut between pairs.
-            if (qvalid) {
-                if (complete) {
-                    uint32_t* oid = p.out_ids + static_cast<uint64_t>(qlocal) * p.k;
-                    float* odist = p.out_dists + static_cast<uint64_t>(qlocal) * p.k;
-                    bool inexact;
-                    if constexpr (kL2) {
-                        inexact = static_cast<int64_t>(qnorm) + tk.thr() >= (1 << 24);
-                        tk.for_each(p.k, [&](int jj, int32_t key, uint32_t id) {
-                            oid[jj] = id;
-                            odist[jj] = __int2float_rn(qnorm + key);
-                        });
-                    } else {
-                        inexact = -static_cast<int64_t>(tk.best(p.k)) >= (1 << 24);
-                        tk.for_each(p.k, [&](int jj, int32_t key, uint32_t id) {
-                            oid[jj] = id;
-                            odist[jj] = -__int2float_rn(-key);
-                        });
+            if constexpr (kSlices > 1) {
+                // The four slices' lists of each row meet in slice 0 (named
+                // barrier per lane quarter: its four warps): slices 1 and 3
+                // hand their lists to slices 0 and 2, then slice 2 to 0.
+                int32_t* m0 = sMerge + (0 * kTileRows + row) * 2 * kMergeCap;
+                int32_t* m1 = sMerge + (1 * kTileRows + row) * 2 * kMergeCap;
+                auto put = [&](int32_t* m) {
+                    tk.for_each(p.k, [&](int jj, int32_t key, uint32_t id) {
+                        m[jj] = key;
+                        m[kMergeCap + jj] = static_cast<int32_t>(id);
+                    });
+                };
+                auto take = [&](const int32_t* m) {
+                    for (uint32_t jj = 0; jj < p.k; ++jj) {
+                        const int32_t key = m[jj];
+                        const uint32_t id = static_cast<uint32_t>(m[kMergeCap + jj]);
+                        if (key_gt(tk.thr(), tk.thr_id(), key, id)) tk.insert(key, id);
                     }
-                    if (inexact) {
-                        const uint32_t fs = atomicAdd(p.fallback_count, 1u);
-                        p.fallback_rows[fs] = qlocal;
+                };
+                auto group_sync = [&]() -> bool {
+                    merge_round += kSlices;
+                    __syncwarp();
+                    if (lane == 0) {
+                        __threadfence_block();
+                        atomicAdd(&merge_cnt[quarter], 1u);
                     }
+                    const bool r = spin_until_geq(reinterpret_cast<volatile uint32_t*>(&merge_cnt[quarter]),
+                                                  merge_round, abort_flag, 32, lim_cycles);
+                    __threadfence_block();
+                    return __all_sync(0xffffffffu, r);
+                };
+                if constexpr (kSlices == 4) {
+                    if (slice == 1) put(m0);
+                    if (slice == 3) put(m1);
+                    ok = group_sync();
+                    if (ok && slice == 0) take(m0);
+                    if (ok && slice == 2) take(m1);
+                    ok = ok && group_sync();
+                    if (ok && slice == 2) put(m0);
+                    ok = ok && group_sync();
+                    if (ok && slice == 0) take(m0);
+                    ok = ok && group_sync();
                 } else {
-                    const uint32_t pslot = 2 * pair + (seg_lo == w0 ? 0u : 1u);
+                    (void)m1;
+                    if (slice == 1) put(m0);
+                    ok = group_sync();
+                    if (ok && slice == 0) take(m0);
+                    ok = ok && group_sync();
+                }
+                if (!ok) break;
+            }
+            // Segment done (slice 0): final graph rows, or a partial list of a
+            // query tile cut between pairs; in the seeding pass only the k-th key.
+            if (qvalid && slice == 0) {
+                if (complete && p.seed_out) {
+                    p.seed_out[qlocal] = tk.thr();
+                } else if (complete) {
+                    const int32_t qnorm =
+                        kL2 ? packed_sq_norm(p.query_packed, p.pitch, p.data_bytes, p.query_norms, qlocal) : 0;
+                    emit_graph_row<METRIC>(tk, p.k, qlocal, qnorm, p.out_ids, p.out_dists, p.fallback_rows,
+                                           p.fallback_count);
+                } else {
                     const uint64_t o = (static_cast<uint64_t>(pslot) * kPairTile + cta * kTileRows + row) * p.k;
                     tk.for_each(p.k, [&](int jj, int32_t key, uint32_t id) {
                         p.part_keys[o + jj] = key;
@@ -589,10 +606,13 @@ __global__ void __launch_bounds__(kPairThreads, 1) knn_pair_kernel(const __grid_
                     });
                 }
             }
-            if (bt == nbt) {
-                bt = 0;
-                ++qt;
-            }
+        }
+        if (prof) {
+            atomicAdd(p.debug_clocks + 0, static_cast<unsigned long long>(c_tf));
+            atomicAdd(p.debug_clocks + 1, static_cast<unsigned long long>(c_slow));
+            atomicAdd(p.debug_clocks + 2, n_slow);
+            atomicAdd(p.debug_clocks + 3, static_cast<unsigned long long>(clock64() - c_t0));
+            atomicAdd(p.debug_clocks + 7, n_slow_calls);
         }
         if (!ok) abort_pair(4);
     }
@@ -605,84 +625,6 @@ __global__ void __launch_bounds__(kPairThreads, 1) knn_pair_kernel(const __grid_
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc_pair(tmem_base, 512);
-    }
-}
-
-// The pair holding work item w (largest p with pair_work_begin(p) <= w).
-__device__ inline uint32_t pair_of_work(uint64_t total, uint32_t n_pairs, uint64_t w)
-{
-    uint32_t p = static_cast<uint32_t>(w * n_pairs / total);
-    while (p + 1 < n_pairs && pair_work_begin(total, n_pairs, p + 1) <= w) ++p;
-    while (p > 0 && pair_work_begin(total, n_pairs, p) > w) --p;
-    return p;
-}
-
-// Merge the partial lists of query tiles cut between pairs. Block b looks at
-// the boundary between pairs b and b + 1; it handles the query tile that
-// boundary falls inside (if it does not fall on a tile start), unless the
-// previous boundary cut the same tile. One thread per query row.
-template <int METRIC, int KCAP>
-__global__ void __launch_bounds__(kPairTile) merge_pair_partials(const PairParams p)
-{
-    const uint32_t pb = blockIdx.x + 1;  // boundary: start of pair pb
-    if (pb >= p.n_pairs || (p.skip_flag && *p.skip_flag)) return;
-    const uint32_t nbt = p.n_btiles;
-    const uint64_t wb = pair_work_begin(p.total, p.n_pairs, pb);
-    if (wb % nbt == 0) return;
-    const uint32_t q = static_cast<uint32_t>(wb / nbt);
-    if (pb > 1) {
-        const uint64_t wprev = pair_work_begin(p.total, p.n_pairs, pb - 1);
-        if (wprev / nbt == q && wprev % nbt != 0) return;
-    }
-    const uint64_t qlo = static_cast<uint64_t>(q) * nbt, qhi = qlo + nbt;
-    const uint32_t p_first = pair_of_work(p.total, p.n_pairs, qlo);
-    const uint32_t p_last = pair_of_work(p.total, p.n_pairs, qhi - 1);
-    const uint32_t r = threadIdx.x;
-    const uint32_t qlocal = q * kPairTile + r;
-    if (qlocal >= p.n_queries) return;
-    RegTopK<KCAP> tk;
-    tk.init(p.k);
-    for (uint32_t pp = p_first; pp <= p_last; ++pp) {
-        const uint32_t slot = (pp == p_first && pair_work_begin(p.total, p.n_pairs, pp) != qlo) ? 1u : 0u;
-        const uint64_t o = (static_cast<uint64_t>(2 * pp + slot) * kPairTile + r) * p.k;
-        for (uint32_t j = 0; j < p.k; ++j) {
-            const int32_t key = p.part_keys[o + j];
-            const uint32_t id = p.part_ids[o + j];
-            if (key_gt(tk.thr(), tk.thr_id(), key, id)) tk.insert(key, id);
-        }
-    }
-    uint32_t* oid = p.out_ids + static_cast<uint64_t>(qlocal) * p.k;
-    float* odist = p.out_dists + static_cast<uint64_t>(qlocal) * p.k;
-    bool inexact;
-    if constexpr (METRIC == 0) {
-        const uint4* a4 = reinterpret_cast<const uint4*>(p.query_packed + static_cast<uint64_t>(qlocal) * p.pitch +
-                                                         p.data_bytes);
-        const uint4 x0 = a4[0], x1 = a4[1];
-        uint32_t sb = 0;
-        sb = __dp4a(x0.x, 0x01010101u, sb);
-        sb = __dp4a(x0.y, 0x01010101u, sb);
-        sb = __dp4a(x0.z, 0x01010101u, sb);
-        sb = __dp4a(x0.w, 0x01010101u, sb);
-        sb = __dp4a(x1.x, 0x01010101u, sb);
-        sb = __dp4a(x1.y, 0x01010101u, sb);
-        sb = __dp4a(x1.z, 0x01010101u, sb);
-        sb = __dp4a(x1.w, 0x01010101u, sb);
-        const int32_t qnorm = p.query_norms[qlocal] - 510 * static_cast<int32_t>(sb);
-        inexact = static_cast<int64_t>(qnorm) + tk.thr() >= (1 << 24);
-        tk.for_each(p.k, [&](int jj, int32_t key, uint32_t id) {
-            oid[jj] = id;
-            odist[jj] = __int2float_rn(qnorm + key);
-        });
-    } else {
-        inexact = -static_cast<int64_t>(tk.best(p.k)) >= (1 << 24);
-        tk.for_each(p.k, [&](int jj, int32_t key, uint32_t id) {
-            oid[jj] = id;
-            odist[jj] = -__int2float_rn(-key);
-        });
-    }
-    if (inexact) {
-        const uint32_t fs = atomicAdd(p.fallback_count, 1u);
-        p.fallback_rows[fs] = qlocal;
     }
 }
 

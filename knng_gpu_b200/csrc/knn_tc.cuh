@@ -32,6 +32,7 @@
 #include <type_traits>
 
 #include "ptx.cuh"
+#include "schedule.cuh"
 #include "topk.cuh"
 
 namespace knng_b200 {
@@ -98,6 +99,11 @@ struct KnnTcParams {
     uint32_t* fallback_rows;     // u8: rows whose fp32 sums may be inexact
     uint32_t* fallback_count;
     int* error;                  // non-zero: a bounded wait gave up
+    TileSchedule sched;          // units = CTAs; MT*128-row query tiles, 128-row base tiles
+    int32_t* part_keys;          // u8: [2 * n_units][MT*128][k] partial lists of cut query tiles
+    uint32_t* part_ids;
+    uint32_t part_units;         // units whose partial lists fit (0: whole query tiles only)
+    const int* skip_flag;        // u8: non-zero -> the data is not integer-valued, do nothing
     uint32_t debug_flags;        // profiling only: 1 skip filtering, 2 skip insertion, 4 skip TMEM loads
     unsigned long long* debug_clocks;  // profiling only: per-role wait cycles (flag 512)
 };
@@ -190,6 +196,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
     static_assert(SPLIT == 1 || (SPLIT == 2 && TopK::kRegs <= 32 && !kPerMtBars), "split epilogue");
     constexpr int kCap = TopK::kRegs / 2;
 
+    if (p.skip_flag && *p.skip_flag) return;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     // u8 L2: the K dimension is extended by 32 bytes so that the accumulator
@@ -227,8 +234,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const uint32_t n_qtiles = (p.n_queries + MT * kTileRows - 1) / (MT * kTileRows);
-    const uint32_t n_btiles = static_cast<uint32_t>((p.n_base + BN - 1) / BN);
+    const uint32_t unit = blockIdx.x;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S; ++s) {
@@ -279,7 +285,8 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
             const bool dbg = (p.debug_flags & 512u) && p.debug_clocks;
             const bool no_tma = (p.debug_flags & 2048u) != 0;  // profiling only
             long long c_wait = 0, c_start = clock64();
-            for (uint32_t t = blockIdx.x; t < n_qtiles && ok; t += gridDim.x) {
+            uint32_t t, b0, b1, pslot;
+            for (uint32_t sg = 0; ok && schedule_segment(p.sched, unit, sg, t, b0, b1, pslot); ++sg) {
                 if (!A_STREAM) {
                     ok = mbar_wait(a_empty, a_par ^ 1, abort_flag);
                     if (!ok) break;
@@ -292,7 +299,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                                             kc * kChunkBytes / (Elem::kFloat ? 2 : 1),
                                             p.query_row0 + (t * MT + mt) * kTileRows, a_full);
                 }
-                for (uint32_t j = 0; j < n_btiles && ok; ++j) {
+                for (uint32_t j = b0; j < b1 && ok; ++j) {
                     for (uint32_t kc = 0; kc < p.kchunks; ++kc) {
                         if (stage_commits) {
                             ok = mbar_wait(&empty[stage], phase ^ 1, abort_flag);
@@ -400,7 +407,10 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                     if (kc + 1 == p.kchunks) umma_u8(d_tmem, a_aug_desc, b_aug_desc0 + stage * stage_step, idesc, 1u);
                 }
             };
-            for (uint32_t t = blockIdx.x; t < n_qtiles && ok; t += gridDim.x) {
+            uint32_t t, b0, b1, pslot;
+            for (uint32_t sg = 0; ok && schedule_segment(p.sched, unit, sg, t, b0, b1, pslot); ++sg) {
+                (void)t;
+                (void)pslot;
                 if (!A_STREAM) {
                     ok = mbar_wait(a_full, a_par, abort_flag);
                     if (!ok) break;
@@ -411,7 +421,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                     // Hot configuration (one K chunk, resident A, two TMEM
                     // buffers, stages released by counter): per tile two waits,
                     // one fence, the MMAs as straight-line code, one commit.
-                    for (uint32_t j = 0; j < n_btiles; ++j, ++acc_i) {
+                    for (uint32_t j = b0; j < b1; ++j, ++acc_i) {
                         const uint32_t buf = acc_i & 1u;
                         const uint32_t tpar = ((acc_i >> 1) & 1u) ^ 1u;
                         if (!mbar_wait_sleep(&full[s], ph, abort_flag) ||
@@ -447,7 +457,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                         if constexpr (!kSplitHandoff) umma_commit(&tfull[buf]);
                     }
                 }
-                for (uint32_t j = 0; !lean && j < n_btiles && ok; ++j, ++acc_i) {
+                for (uint32_t j = b0; !lean && j < b1 && ok; ++j, ++acc_i) {
                     const uint32_t buf = NBUF == 1 ? 0u : acc_i & (NBUF - 1);
                     const uint32_t tpar = (acc_i / NBUF) & 1;
                     if (kPerMtBars) {
@@ -600,7 +610,9 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
         bool ok = true;
         const bool dbg = (p.debug_flags & 512u) && p.debug_clocks && ew == 0 && lane == 0;
         long long c_tfull = 0, c_start = clock64();
-        for (uint32_t t = blockIdx.x; t < n_qtiles && ok; t += gridDim.x, ++qt_iter) {
+        uint32_t t, b0, b1, pslot;
+        for (uint32_t sg = 0; ok && schedule_segment(p.sched, unit, sg, t, b0, b1, pslot); ++sg, ++qt_iter) {
+            const bool complete = b0 == 0 && b1 == p.sched.n_btiles;
             const uint32_t qlocal = (t * MT + mt) * kTileRows + row;
             const bool qvalid = qlocal < p.n_queries;
             const uint32_t self_id = p.exclude_self ? p.query_id0 + qlocal : UINT32_MAX;
@@ -638,15 +650,15 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                 }
             };
             __syncwarp();
-            for (uint32_t jj = 0; jj + 1 < kNormRing; ++jj) {
-                if (jj < n_btiles) fetch_norms(jj);
+            for (uint32_t jj = b0; jj + 1 < b0 + kNormRing; ++jj) {
+                if (jj < b1) fetch_norms(jj);
                 cp_async_commit();
             }
-            for (uint32_t j = 0; j < n_btiles; ++j, ++acc_i) {
+            for (uint32_t j = b0; j < b1; ++j, ++acc_i) {
                 // Every lane is done with tile j-1, whose slot now receives
                 // tile j + kNormRing - 1; then wait for tile j's copies.
                 __syncwarp();
-                if (j + kNormRing - 1 < n_btiles) fetch_norms(j + kNormRing - 1);
+                if (j + kNormRing - 1 < b1) fetch_norms(j + kNormRing - 1);
                 cp_async_commit();
                 cp_async_wait_group<kNormRing - 1>();
                 finish_norms(j);
@@ -841,6 +853,14 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                 tk.for_each(p.k, [&](int jj, int32_t key, uint32_t id) {
                     oid[jj] = id;
                     okey[jj] = key;
+                });
+            } else if (!complete) {
+                // A piece of a tail query tile cut between CTAs: its partial
+                // list, merged with the other pieces' afterwards.
+                const uint64_t o = (static_cast<uint64_t>(pslot) * (MT * kTileRows) + mt * kTileRows + row) * p.k;
+                tk.for_each(p.k, [&](int jj, int32_t key, uint32_t id) {
+                    p.part_keys[o + jj] = key;
+                    p.part_ids[o + jj] = id;
                 });
             } else {
                 float* odist = p.out_dists + static_cast<uint64_t>(qlocal) * p.k;

@@ -278,27 +278,37 @@ int sm_count()
 
 // ------------------------------------------------------------------ launch helpers
 // Scratch of a u8 search: the fallback-row list (one entry per query), two
-// counters (fallback count, error word), then the partial (key, id) lists of
-// query tiles that the pair kernel cuts between CTA pairs (two lists of 256
-// rows x k per pair). Without the partial region the single-CTA kernel runs.
+// counters (fallback count, error word), the seeded bounds (one per query),
+// then the partial (key, id) lists of tail query tiles cut between units
+// (two lists of up to 256 rows x k per unit). Without the partial region the
+// single-CTA kernel searches whole query tiles only and the pair kernel is
+// not used.
 struct ScratchU8 {
     uint32_t* fallback_rows;
     uint32_t* counters;  // [0] fallback count, [1] error flag
+    int32_t* seeds;      // per query: seeded bound on its k-th key (pair kernel)
     int32_t* part_keys;
     uint32_t* part_ids;
-    uint32_t part_pairs;  // CTA pairs whose partial lists fit
+    uint32_t part_units;  // units (CTAs or CTA pairs) whose partial lists fit (0: none)
 };
 
-// CTA pairs a device can hold at once (one pair per two SMs).
-uint32_t max_pairs() { return static_cast<uint32_t>(std::max(1, sm_count() / 2)); }
+// Seeding pass of the pair kernel: the first kSeedRows base rows, used when
+// the base holds at least kSeedMinBase rows.
+constexpr uint64_t kSeedRows = 16384;
+constexpr uint64_t kSeedMinBase = 8 * kSeedRows;
 
-uint64_t partial_bytes_per_pair(uint64_t k) { return 2ull * kPairTile * k * 8; }
+// Units of a persistent launch: at most one CTA per SM.
+uint32_t max_units() { return static_cast<uint32_t>(std::max(1, sm_count())); }
+
+// Two partial lists of one 256-row query tile per unit.
+uint64_t partial_bytes_per_unit(uint64_t k) { return 2ull * 256 * k * 8; }
 
 uint64_t scratch_u8_base_bytes(uint64_t q_count) { return align_up(q_count * 4, 256) + 256; }
 
 uint64_t scratch_u8_bytes(uint64_t q_count, uint64_t k)
 {
-    return scratch_u8_base_bytes(q_count) + align_up(max_pairs() * partial_bytes_per_pair(k), 256);
+    return scratch_u8_base_bytes(q_count) + align_up(q_count * 4, 256) +
+           align_up(max_units() * partial_bytes_per_unit(k), 256);
 }
 
 ScratchU8 carve_scratch_u8(void* p, uint64_t q_count, uint64_t k, uint64_t bytes)
@@ -307,12 +317,13 @@ ScratchU8 carve_scratch_u8(void* p, uint64_t q_count, uint64_t k, uint64_t bytes
     uint8_t* b = static_cast<uint8_t*>(p);
     s.fallback_rows = reinterpret_cast<uint32_t*>(b);
     s.counters = reinterpret_cast<uint32_t*>(b + align_up(q_count * 4, 256));
-    const uint64_t base = scratch_u8_base_bytes(q_count);
+    s.seeds = reinterpret_cast<int32_t*>(b + scratch_u8_base_bytes(q_count));
+    const uint64_t base = scratch_u8_base_bytes(q_count) + align_up(q_count * 4, 256);
     const uint64_t rest = bytes > base ? bytes - base : 0;
-    const uint64_t per_pair = partial_bytes_per_pair(k);
-    s.part_pairs = static_cast<uint32_t>(std::min<uint64_t>(rest / per_pair, 1u << 16));
+    const uint64_t per_unit = partial_bytes_per_unit(k);
+    s.part_units = static_cast<uint32_t>(std::min<uint64_t>(rest / per_unit, 1u << 16));
     s.part_keys = reinterpret_cast<int32_t*>(b + base);
-    s.part_ids = reinterpret_cast<uint32_t*>(b + base + s.part_pairs * per_pair / 2);
+    s.part_ids = reinterpret_cast<uint32_t*>(b + base + s.part_units * per_unit / 2);
     return s;
 }
 
@@ -320,8 +331,12 @@ struct TcMaps {
     CUtensorMap q0, q1, b0, b1;
 };
 
+// Persistent launch, one CTA per SM. u8 with register lists and partial-list
+// scratch: whole query tiles in full waves, the last partial wave cut into
+// equal ranges and merged afterwards (schedule.cuh); otherwise whole query
+// tiles round-robin.
 template <class Elem, int MT, int NBUF, bool A_STREAM, int METRIC, class TopK, int SPLIT = 1>
-knng_gpu_status launch_tc_t(const TcMaps& m, const KnnTcParams& p, cudaStream_t st)
+knng_gpu_status launch_tc_t(const TcMaps& m, KnnTcParams p, cudaStream_t st)
 {
     const SmemLayoutTc L = smem_layout_tc(Elem::kPlanes, MT, A_STREAM, p.kchunks, p.stages, SPLIT,
                                           SPLIT > 1 ? TopK::kRegs / 2 : 0, !Elem::kFloat && METRIC == 0);
@@ -329,10 +344,41 @@ knng_gpu_status launch_tc_t(const TcMaps& m, const KnnTcParams& p, cudaStream_t 
     auto kern = knn_tc_kernel<Elem, MT, NBUF, A_STREAM, METRIC, TopK, SPLIT>;
     KNNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const uint32_t n_qtiles = (p.n_queries + MT * kTileRows - 1) / (MT * kTileRows);
-    uint32_t grid = std::min<uint32_t>(n_qtiles, static_cast<uint32_t>(sm_count()));
-    if (const char* gv = experiment_knob("KNNG_GPU_GRID")) grid = std::min<uint32_t>(grid, std::max(1, std::atoi(gv)));  // experiments only
-    kern<<<grid, 64 + 128 * MT * SPLIT, smem, st>>>(m.q0, m.q1, m.b0, m.b1, p);
+    const uint32_t n_btiles = static_cast<uint32_t>((p.n_base + kTileRows - 1) / kTileRows);
+    uint32_t units = static_cast<uint32_t>(sm_count());
+    if (const char* gv = experiment_knob("KNNG_GPU_GRID")) units = std::min<uint32_t>(units, std::max(1, std::atoi(gv)));
+    bool tail = !Elem::kFloat && TopK::kCap > 0 && p.part_keys != nullptr && p.part_units >= units;
+    if (const char* tv = experiment_knob("KNNG_GPU_TAIL_SPLIT")) tail = tail && std::atoi(tv) != 0;
+    if (tail) {
+        if (n_qtiles < units) units = static_cast<uint32_t>(std::min<uint64_t>(units, uint64_t(n_qtiles) * n_btiles));
+    } else {
+        units = std::min<uint32_t>(units, n_qtiles);
+    }
+    p.sched = make_schedule(units, n_qtiles, n_btiles, !tail);
+    kern<<<units, 64 + 128 * MT * SPLIT, smem, st>>>(m.q0, m.q1, m.b0, m.b1, p);
     KNNG_CUDA(cudaGetLastError());
+    if constexpr (!Elem::kFloat && TopK::kCap > 0) {
+        if (tail && units > 1 && p.sched.tail_total > 0) {
+            MergeParams mp{};
+            mp.s = p.sched;
+            mp.qtile_rows = MT * kTileRows;
+            mp.k = p.k;
+            mp.n_queries = p.n_queries;
+            mp.part_keys = p.part_keys;
+            mp.part_ids = p.part_ids;
+            mp.out_ids = p.out_ids;
+            mp.out_dists = p.out_dists;
+            mp.query_norms = p.query_norms;
+            mp.query_packed = p.query_packed;
+            mp.pitch = p.pitch;
+            mp.data_bytes = p.data_bytes;
+            mp.fallback_rows = p.fallback_rows;
+            mp.fallback_count = p.fallback_count;
+            mp.skip_flag = p.skip_flag;
+            merge_partials<METRIC, TopK::kCap><<<units - 1, MT * kTileRows, 0, st>>>(mp);
+            KNNG_CUDA(cudaGetLastError());
+        }
+    }
     return KNNG_GPU_OK;
 }
 
@@ -489,7 +535,8 @@ int u8_query_tiles_per_cta(uint64_t d, uint64_t k)
 // caller zeroes sc.counters before and reads them after. tf (optional) times
 // the exact pass.
 knng_gpu_status launch_u8_sets(const U8Sets& z, uint64_t d, uint64_t k, int metric, uint32_t* ids, float* dists,
-                               const ScratchU8& sc, cudaStream_t st, uint32_t* launches, EventTimer* tf)
+                               const ScratchU8& sc, cudaStream_t st, uint32_t* launches, EventTimer* tf,
+                               const int* skip_flag = nullptr)
 {
     const uint64_t q_count = z.n_q;
     const uint64_t pitch = knng_gpu_padded_dim(d);
@@ -538,6 +585,10 @@ knng_gpu_status launch_u8_sets(const U8Sets& z, uint64_t d, uint64_t k, int metr
         p.fallback_rows = sc.fallback_rows;
         p.fallback_count = sc.counters;
         p.error = reinterpret_cast<int*>(sc.counters + 1);
+        p.part_keys = sc.part_keys;
+        p.part_ids = sc.part_ids;
+        p.part_units = sc.part_units;
+        p.skip_flag = skip_flag;
         if (const char* dbg = experiment_knob("KNNG_GPU_DEBUG_FLAGS")) p.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
         int mt = u8_query_tiles_per_cta(d, k);
         // Optional column-split epilogue (four epilogue warps per SM
@@ -604,13 +655,13 @@ struct PairMaps {
     CUtensorMap q, b, baug, norm;
 };
 
-template <int METRIC, int KC>
+template <int METRIC, int KC, int EPI>
 knng_gpu_status launch_pair_t(const PairMaps& m, PairParams& pp, uint32_t max_pairs_fit, cudaStream_t st,
                               uint32_t* launches, EventTimer* tt)
 {
-    const SmemLayoutPair L = smem_layout_pair(pp.kchunks, pp.stages, METRIC == 0);
+    const SmemLayoutPair L = smem_layout_pair(pp.kchunks, pp.stages, METRIC == 0, EPI > 4 ? KC : 0);
     const uint32_t smem = L.total + 1024;
-    auto kern = knn_pair_kernel<METRIC, RegTopK<KC>>;
+    auto kern = knn_pair_kernel<METRIC, RegTopK<KC>, EPI>;
     KNNG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -618,46 +669,108 @@ knng_gpu_status launch_pair_t(const PairMaps& m, PairParams& pp, uint32_t max_pa
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.blockDim = dim3(kPairThreads);
+    cfg.blockDim = dim3(pair_threads(EPI));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cfg.gridDim = dim3(2 * max_pairs());
+    cfg.gridDim = dim3(2 * (max_units() / 2));
     int clusters = 0;
     KNNG_CUDA(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
     uint64_t np = std::min<uint64_t>(static_cast<uint64_t>(std::max(clusters, 0)), max_pairs_fit);
-    np = std::min<uint64_t>(np, pp.total);
     if (const char* gv = experiment_knob("KNNG_GPU_PAIRS")) np = std::min<uint64_t>(np, std::max(1, std::atoi(gv)));
+    // Whole query tiles in full waves over all pairs, the last partial wave
+    // cut into equal ranges (few queries: only that).
+    const uint64_t nqt = pp.sched.n_qtiles, nbt = pp.sched.n_btiles;
+    if (nqt < np) np = std::min<uint64_t>(np, nqt * nbt);
     if (np == 0) return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: no CTA pair fits on this device");
-    pp.n_pairs = static_cast<uint32_t>(np);
-    cfg.gridDim = dim3(2 * pp.n_pairs);
+    pp.sched = make_schedule(static_cast<uint32_t>(np), static_cast<uint32_t>(nqt), static_cast<uint32_t>(nbt), false);
+    unsigned long long* dbg_clk = nullptr;
+    if (kExperiments && (pp.debug_flags & 512u)) {  // profiling only
+        cudaMalloc(&dbg_clk, 16 * sizeof(unsigned long long));
+        cudaMemsetAsync(dbg_clk, 0, 16 * sizeof(unsigned long long), st);
+        pp.debug_clocks = dbg_clk;
+    }
     if (tt) tt->start(st);
     KNNG_CUDA(cudaLaunchKernelEx(&cfg, kern, m.q, m.b, m.baug, m.norm, pp));
     if (tt) tt->stop(st);
     ++*launches;
-    if (pp.n_pairs > 1) {
-        merge_pair_partials<METRIC, KC><<<pp.n_pairs - 1, kPairTile, 0, st>>>(pp);
+    if (dbg_clk) {
+        unsigned long long h[16];
+        cudaMemcpyAsync(h, dbg_clk, sizeof(h), cudaMemcpyDeviceToHost, st);
+        cudaStreamSynchronize(st);
+        const double warps = 2.0 * pp.sched.n_units * EPI;
+        std::fprintf(stderr,
+                     "pair clocks per epilogue warp: wait_tfull %.3g slow %.3g n_slow %.3g n_slow_calls %.3g total %.3g | "
+                     "per MMA thread: wait_tempty %.3g wait_full %.3g total %.3g | tiles per pair %.3g\n",
+                     h[0] / warps, h[1] / warps, h[2] / warps, h[7] / warps, h[3] / warps,
+                     h[4] / double(pp.sched.n_units), h[5] / double(pp.sched.n_units),
+                     h[6] / double(pp.sched.n_units),
+                     double(pp.sched.n_qtiles) * pp.sched.n_btiles / pp.sched.n_units);
+        cudaFree(dbg_clk);
+    }
+    if (pp.sched.n_units > 1 && pp.sched.tail_total > 0) {
+        MergeParams mp{};
+        mp.s = pp.sched;
+        mp.qtile_rows = kPairTile;
+        mp.k = pp.k;
+        mp.n_queries = pp.n_queries;
+        mp.part_keys = pp.part_keys;
+        mp.part_ids = pp.part_ids;
+        mp.out_ids = pp.out_ids;
+        mp.out_dists = pp.out_dists;
+        mp.seed_out = pp.seed_out;
+        mp.query_norms = pp.query_norms;
+        mp.query_packed = pp.query_packed;
+        mp.pitch = pp.pitch;
+        mp.data_bytes = pp.data_bytes;
+        mp.fallback_rows = pp.fallback_rows;
+        mp.fallback_count = pp.fallback_count;
+        mp.skip_flag = pp.skip_flag;
+        merge_partials<METRIC, KC><<<pp.sched.n_units - 1, kPairTile, 0, st>>>(mp);
         KNNG_CUDA(cudaGetLastError());
         ++*launches;
     }
     return KNNG_GPU_OK;
 }
 
+// Sixteen epilogue warps (four 64-column slices per lane quarter) for short
+// tiles (d <= 256, where the tensor core finishes a tile in ~1000 cycles)
+// and small lists; four otherwise.
+int pair_epi_warps(uint32_t kchunks, uint64_t k)
+{
+    int epi = (kchunks <= 2 && k <= 16) ? 16 : 4;
+    if (const char* ev = experiment_knob("KNNG_GPU_EPI")) {
+        const int e = std::atoi(ev);
+        if (e == 4 || e == 8) epi = e;
+    }
+    return epi;
+}
+
 template <int METRIC>
 knng_gpu_status launch_pair_k(const PairMaps& m, PairParams& pp, uint32_t fit, cudaStream_t st, uint32_t* launches,
                               EventTimer* tt)
 {
-    if (pp.k <= 10) return launch_pair_t<METRIC, 10>(m, pp, fit, st, launches, tt);
-    if (pp.k <= 16) return launch_pair_t<METRIC, 16>(m, pp, fit, st, launches, tt);
-    if (pp.k <= 32) return launch_pair_t<METRIC, 32>(m, pp, fit, st, launches, tt);
-    return launch_pair_t<METRIC, 64>(m, pp, fit, st, launches, tt);
+    const int epi = pair_epi_warps(pp.kchunks, pp.k);
+    if (epi == 16) {
+        if (pp.k <= 10) return launch_pair_t<METRIC, 10, 16>(m, pp, fit, st, launches, tt);
+        return launch_pair_t<METRIC, 16, 16>(m, pp, fit, st, launches, tt);
+    }
+    if (kExperiments && epi == 8) {
+        if (pp.k <= 10) return launch_pair_t<METRIC, 10, 8>(m, pp, fit, st, launches, tt);
+        return launch_pair_t<METRIC, 16, 8>(m, pp, fit, st, launches, tt);
+    }
+    if (pp.k <= 10) return launch_pair_t<METRIC, 10, 4>(m, pp, fit, st, launches, tt);
+    if (pp.k <= 16) return launch_pair_t<METRIC, 16, 4>(m, pp, fit, st, launches, tt);
+    if (pp.k <= 32) return launch_pair_t<METRIC, 32, 4>(m, pp, fit, st, launches, tt);
+    return launch_pair_t<METRIC, 64, 4>(m, pp, fit, st, launches, tt);
 }
 
 // Stages of the pair kernel that fit the shared-memory budget (0: none).
-uint32_t pick_pair_stages(uint32_t kchunks, bool l2)
+uint32_t pick_pair_stages(uint32_t kchunks, bool l2, uint64_t k)
 {
-    const SmemLayoutPair L0 = smem_layout_pair(kchunks, 0, l2);
+    const uint32_t merge_cap = (pair_epi_warps(kchunks, k) > 4 && k <= 16) ? (k <= 10 ? 10 : 16) : 0;
+    const SmemLayoutPair L0 = smem_layout_pair(kchunks, 0, l2, merge_cap);
     const uint32_t budget = 227u * 1024u - 1024u;
     if (L0.total >= budget) return 0;
     uint32_t s = std::min<uint32_t>(16, (budget - L0.total) / L0.stage_bytes);
@@ -696,10 +809,9 @@ knng_gpu_status launch_u8_pair(const U8Sets& z, uint64_t d, uint64_t k, int metr
     pp.exclude_self = z.exclude_self;
     pp.k = static_cast<uint32_t>(k);
     pp.kchunks = static_cast<uint32_t>(data_bytes / kChunkBytes);
-    pp.stages = pick_pair_stages(pp.kchunks, metric == 0);
-    pp.n_qtiles = static_cast<uint32_t>((z.n_q + kPairTile - 1) / kPairTile);
-    pp.n_btiles = static_cast<uint32_t>((z.n_b + kPairTile - 1) / kPairTile);
-    pp.total = static_cast<uint64_t>(pp.n_qtiles) * pp.n_btiles;
+    pp.stages = pick_pair_stages(pp.kchunks, metric == 0, k);
+    pp.sched = make_schedule(1, static_cast<uint32_t>((z.n_q + kPairTile - 1) / kPairTile),
+                             static_cast<uint32_t>((z.n_b + kPairTile - 1) / kPairTile), false);
     pp.out_ids = ids;
     pp.out_dists = dists;
     pp.part_keys = sc.part_keys;
@@ -711,8 +823,37 @@ knng_gpu_status launch_u8_pair(const U8Sets& z, uint64_t d, uint64_t k, int metr
     pp.test_mode = opt.test_mode;
     pp.skip_flag = opt.skip_flag;
     if (const char* dbg = experiment_knob("KNNG_GPU_DEBUG_FLAGS")) pp.debug_flags = static_cast<uint32_t>(std::atoi(dbg));
-    KNNG_TRY(metric == 0 ? launch_pair_k<0>(m, pp, sc.part_pairs, st, launches, tt)
-                         : launch_pair_k<1>(m, pp, sc.part_pairs, st, launches, tt));
+    if (tt) tt->start(st);
+    // Seeding pass: the queries against the first kSeedRows base rows give
+    // each query an exact upper bound on its k-th key over the whole base
+    // (its k-th key among a subset of the rows). The main pass then admits
+    // only keys at or below that bound, so the top-k lists see far fewer
+    // insertions; the result is unchanged.
+    bool seeded = z.n_b >= kSeedMinBase && k + 1 <= kSeedRows && opt.test_mode == 0;
+    if (const char* sv = experiment_knob("KNNG_GPU_SEED")) seeded = seeded && std::atoi(sv) != 0;
+    if (seeded) {
+        PairMaps ms = m;
+        KNNG_TRY(make_map(&ms.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.b_packed, kSeedRows, data_bytes, pitch));
+        if (metric == 0) {
+            KNNG_TRY(make_map(&ms.baug, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.b_packed + data_bytes, kSeedRows,
+                              kAugBytes, pitch, kAugBytes));
+            KNNG_TRY(make_map_1d_i32(&ms.norm, z.b_norms, kSeedRows, kPairTile));
+        } else {
+            ms.baug = ms.b;
+            ms.norm = ms.b;
+        }
+        PairParams ps = pp;
+        ps.n_base = kSeedRows;
+        ps.sched.n_btiles = static_cast<uint32_t>(kSeedRows / kPairTile);
+        ps.seed_out = sc.seeds;
+        ps.debug_flags = 0;
+        KNNG_TRY(metric == 0 ? launch_pair_k<0>(ms, ps, sc.part_units, st, launches, nullptr)
+                             : launch_pair_k<1>(ms, ps, sc.part_units, st, launches, nullptr));
+        pp.seed_in = sc.seeds;
+    }
+    KNNG_TRY(metric == 0 ? launch_pair_k<0>(m, pp, sc.part_units, st, launches, nullptr)
+                         : launch_pair_k<1>(m, pp, sc.part_units, st, launches, nullptr));
+    if (tt) tt->stop(st);
     // Rows whose fp32 sums may round: recompute exactly (device-side count).
     KnnExactParams<uint8_t> e{};
     e.base = z.b_packed;
@@ -735,15 +876,21 @@ knng_gpu_status launch_u8_pair(const U8Sets& z, uint64_t d, uint64_t k, int metr
     return KNNG_GPU_OK;
 }
 
-// Whether the pair kernel applies: d <= 1024 with a stage budget, k <= 64
-// (register lists), partial-list scratch present, and 16-byte aligned key
-// offsets (TMA source).
+// Whether the pair kernel applies: rows longer than 256 bytes (the pair
+// tile's hand-off costs more than a d <= 256 tile's tensor work; measured on
+// B200: d = 128 searches run faster on the single-CTA kernel at every size,
+// d = 784 ones faster on the pair kernel), d <= 1024 with a stage budget,
+// k <= 64 (register lists), partial-list scratch present, and 16-byte aligned
+// key offsets (TMA source).
 bool pair_applies(const U8Sets& z, uint64_t d, uint64_t k, int metric, const ScratchU8& sc, const U8RunOptions& opt)
 {
-    if (!opt.allow_pair || d > kMaxTensorDim || k > 64 || sc.part_pairs == 0) return false;
-    if (const char* pv = experiment_knob("KNNG_GPU_PAIR")) if (std::atoi(pv) == 0) return false;
+    if (!opt.allow_pair || d > kMaxTensorDim || k > 64 || sc.part_units == 0) return false;
+    const uint32_t kchunks = static_cast<uint32_t>(u8_data_bytes(d) / kChunkBytes);
+    bool want = kchunks >= 3 || opt.test_mode != 0;
+    if (const char* pv = experiment_knob("KNNG_GPU_PAIR")) want = std::atoi(pv) != 0;
+    if (!want) return false;
     if (metric == 0 && (reinterpret_cast<uintptr_t>(z.b_norms) & 15)) return false;
-    return pick_pair_stages(static_cast<uint32_t>(u8_data_bytes(d) / kChunkBytes), metric == 0) >= 2;
+    return pick_pair_stages(kchunks, metric == 0, k) >= 2;
 }
 
 // u8 search of a query set against a base set: the pair kernel where it
@@ -771,7 +918,7 @@ knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int me
         tk.stop(st);
     } else {
         tt.start(st);
-        KNNG_TRY(launch_u8_sets(z, d, k, metric, ids, dists, sc, st, &launches, &tf));
+        KNNG_TRY(launch_u8_sets(z, d, k, metric, ids, dists, sc, st, &launches, &tf, opt.skip_flag));
         tt.stop(st);
         tk.stop(st);
     }
@@ -1231,13 +1378,13 @@ knng_gpu_status device_pipeline(const float* x, uint64_t n, uint64_t d, uint64_t
         std::memset(stats, 0, sizeof(*stats));
         stats->kernel_launches = 2;  // pack + augmentation
     }
-    const U8Sets z{packed, norms, n, 0, packed, norms, n, 0, 1};
     U8RunOptions opt;
     opt.skip_flag = flag;
-    const bool pair = pair_applies(z, d, k, metric, carve_scratch_u8(base + w.scratch, n, k, w.total - w.scratch), opt);
+    // The tensor-core kernels read the flag and return at once for data that
+    // is not integer-valued; the exact-only path (d > 1024) cannot skip.
+    const bool pair = d <= kMaxTensorDim;
     int32_t nonint = 0;
     if (!pair) {
-        // The single-CTA kernel cannot skip itself: read the flag first.
         KNNG_CUDA(cudaMemcpyAsync(&nonint, flag, 4, cudaMemcpyDeviceToHost, st));
         KNNG_CUDA(cudaStreamSynchronize(st));
     }

@@ -341,11 +341,11 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank)
     return r;
 }
 
-// Arrive (release, cluster scope) on an mbarrier given by its shared::cluster
-// address, possibly in the peer CTA.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
+// Arrive on an mbarrier given by its shared::cluster address, possibly in
+// the peer CTA, with the instruction's default semantics (release, CTA scope).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr)
 {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 __device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v)

@@ -195,7 +195,10 @@ knng_gpu_status sharded_replicate(KnngComm* c, const float* slice, uint64_t n, u
     const U8Sets z{packed + sh.start * pitch, norms + sh.start, sh.count, sh.start, packed, norms, n, 0, 1};
     U8RunOptions opt;
     opt.skip_flag = flag;
-    const bool pair = pair_applies(z, d, k, metric, carve_scratch_u8(u + L.scratch, sh.count, k, scratch_u8_bytes(sh.count, k)), opt);
+    // The tensor-core kernels read the reduced flag and return at once for
+    // data that is not integer-valued; only the exact-only path (d > 1024)
+    // needs the flag on the host first.
+    const bool pair = d <= kMaxTensorDim;
     int32_t nonint = 0;
     if (!pair) {
         KNNG_CUDA(cudaMemcpyAsync(&nonint, flag, 4, cudaMemcpyDeviceToHost, st));

@@ -36,6 +36,7 @@ __device__ __forceinline__ float key_to_float(int32_t key)
 template <int KCAP>
 struct RegTopK {
     static constexpr int kRegs = 2 * KCAP;
+    static constexpr int kCap = KCAP;  // register lists: the capacity (merge kernels take it)
     int32_t key[KCAP];
     uint32_t id[KCAP];
 
@@ -114,6 +115,7 @@ struct RegTopK {
 template <int KMAX>
 struct HeapTopK {
     static constexpr int kRegs = 4;
+    static constexpr int kCap = 0;  // not a register list
     int32_t hk[KMAX];
     uint32_t hi[KMAX];
     uint32_t size;

@@ -78,3 +78,27 @@ def test_single_process_multi_gpu_equals_oracle(cuda_ok, ring):
         out = kg.brute_force_knn_multi(y, 7, 0, num_gpus=g)
         oi, od = oracle_knn(y, 7, 0)
         assert np.array_equal(out.neighbors.reshape(-1, 7), oi) and np.array_equal(out.distances.reshape(-1, 7), od)
+
+
+@pytest.mark.parametrize("ring", [False, True])
+def test_sharded_path_on_one_gpu_equals_oracle(cuda_ok, ring):
+    """The multi-GPU code path (knng_gpu_brute_force_multi: NCCL communicator,
+    pack, flag all-reduce, base all-gather or ring pass, gather to rank 0)
+    with a single rank, so it runs on every GPU box; fp32 data goes through
+    the fp32 exchange and path."""
+    import numpy as np
+
+    import knng_gpu_b200 as kg
+    from knng_gpu_b200 import synthetic as syn
+    from refs import oracle_knn
+
+    x = syn.generate(syn.KIND_UNIFORM_INT, 43, 5000, 128)
+    out = kg.brute_force_knn_multi(x, 10, 0, num_gpus=1, ring=ring)
+    oi, od = oracle_knn(x, 10, 0)
+    assert np.array_equal(out.neighbors.reshape(-1, 10), oi)
+    assert np.array_equal(out.distances.reshape(-1, 10), od)
+    if not ring:
+        y = syn.generate(syn.KIND_GAUSSIAN_MIXTURE, 44, 3000, 48, components=8, sigma=0.1)
+        out = kg.brute_force_knn_multi(y, 6, 0, num_gpus=1)
+        oi, od = oracle_knn(y, 6, 0)
+        assert np.array_equal(out.neighbors.reshape(-1, 6), oi) and np.array_equal(out.distances.reshape(-1, 6), od)

@@ -143,11 +143,12 @@ def test_config3_subset_against_oracle(cuda_ok):
 
 
 @pytest.mark.parametrize("metric,k,d", [(0, 10, 128), (1, 10, 128), (0, 32, 200), (1, 64, 784)])
-def test_pair_kernel_matches_single_cta_kernel_and_oracle(cuda_ok, metric, k, d):
-    """The CTA-pair kernel splits the (query tile, base tile) space into equal
-    ranges, so most 256-row query tiles are cut between two pairs and merged
-    afterwards. Every row must equal the single-CTA kernel (which the
-    allocation-free entry point runs), and seeded rows the oracle."""
+def test_scheduled_kernels_match_whole_tile_kernel_and_oracle(cuda_ok, metric, k, d):
+    """knng_gpu_knn_u8 cuts the last wave of query tiles into equal base
+    ranges, one per CTA (d <= 256) or CTA pair (d > 256, the pair kernel, with
+    a seeding pass for large bases), and merges the pieces afterwards. Every
+    row must equal the single-CTA kernel searching whole query tiles (which
+    the allocation-free entry point runs), and seeded rows the oracle."""
     import torch
 
     from knng_gpu_b200 import _native, api
