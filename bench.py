@@ -83,7 +83,9 @@ def describe(cfg) -> dict:
         bf16 = 1590.0
         src = "fallback 1.59 PFLOP/s bf16 burst"
     if integer and cfg.d <= 1024:
-        kernel = "knn_pair_kernel" if cfg.k <= 64 else "knn_tc_kernel<ElemU8>"
+        # The library's selection: the CTA-pair kernel for rows longer than
+        # 256 bytes with k <= 64, the single-CTA kernel otherwise.
+        kernel = "knn_pair_kernel" if (cfg.d > 256 and cfg.k <= 64) else "knn_tc_kernel<ElemU8>"
         peak = 2.0 * bf16
         basis = f"2 x {src} ({bf16} TFLOP/s): the dense int8 tensor rate of B200 is twice its bf16 rate"
         dtype = "u8"
