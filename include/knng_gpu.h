@@ -148,6 +148,9 @@ knng_gpu_status knng_gpu_knn_u8(const uint8_t* d_packed, const int32_t* d_norms,
  *   row r is b_id0 + r, query row i is q_id0 + i; with exclude_self a query
  *   never returns its own id (src/dist/brute_force_mpi.cpp:80-82 excludes by
  *   global index the same way). Needs n_b >= k (+1 with exclude_self).
+ *   d_q_packed, d_b_packed and d_b_norms must be 16-byte aligned (tensor-map
+ *   sources; the key offsets are copied 16 bytes at a time), else
+ *   KNNG_GPU_INVALID_ARGUMENT.
  *   d_scratch: >= knng_gpu_knn_scratch_bytes(n_q, k) bytes, 256-byte aligned.
  * knng_gpu_merge_topk: row-wise merge of two sorted k-lists into the k best
  *   by (distance, id), the TopK order (include/knng/top_k.hpp:56-72); merges

@@ -375,6 +375,7 @@ knng_gpu_status launch_tc_t(const TcMaps& m, KnnTcParams p, cudaStream_t st)
             mp.fallback_rows = p.fallback_rows;
             mp.fallback_count = p.fallback_count;
             mp.skip_flag = p.skip_flag;
+            mp.seed_out = p.seed_out;
             merge_partials<METRIC, TopK::kCap><<<units - 1, MT * kTileRows, 0, st>>>(mp);
             KNNG_CUDA(cudaGetLastError());
         }
@@ -611,12 +612,35 @@ knng_gpu_status launch_u8_sets(const U8Sets& z, uint64_t d, uint64_t k, int metr
             cudaMemsetAsync(dbg_clk, 0, 8 * sizeof(unsigned long long), st);
             p.debug_clocks = dbg_clk;
         }
-        knng_gpu_status s;
-        if (mt == 2)
-            s = metric == 0 ? launch_u8_k<2, 0>(m, p, st, split) : launch_u8_k<2, 1>(m, p, st, split);
-        else
-            s = metric == 0 ? launch_u8_k<1, 0>(m, p, st, split) : launch_u8_k<1, 1>(m, p, st, split);
-        KNNG_TRY(s);
+        auto launch = [&](const TcMaps& mm, const KnnTcParams& pp) {
+            if (mt == 2)
+                return metric == 0 ? launch_u8_k<2, 0>(mm, pp, st, split) : launch_u8_k<2, 1>(mm, pp, st, split);
+            return metric == 0 ? launch_u8_k<1, 0>(mm, pp, st, split) : launch_u8_k<1, 1>(mm, pp, st, split);
+        };
+        // Seeding pass: the queries against the first kSeedRows base rows
+        // give each query an exact upper bound on its k-th key over the whole
+        // base (its k-th key over a subset of the rows); the main pass admits
+        // only keys at or below it. The result is unchanged.
+        bool seeded = z.n_b >= kSeedMinBase && k + 1 <= kSeedRows && k <= 64 && sc.part_units > 0;
+        if (const char* sv = experiment_knob("KNNG_GPU_SEED")) seeded = seeded && std::atoi(sv) != 0;
+        if (seeded) {
+            TcMaps ms = m;
+            KNNG_TRY(make_map(&ms.b0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.b_packed, kSeedRows, data_bytes, pitch));
+            if (metric == 0)
+                KNNG_TRY(make_map(&ms.b1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.b_packed + data_bytes, kSeedRows,
+                                  kAugBytes, pitch, kAugBytes));
+            else
+                ms.b1 = ms.b0;
+            KnnTcParams ps = p;
+            ps.n_base = kSeedRows;
+            ps.seed_out = sc.seeds;
+            ps.debug_flags = 0;
+            ps.debug_clocks = nullptr;
+            KNNG_TRY(launch(ms, ps));
+            *launches += 2;
+            p.seed_in = sc.seeds;
+        }
+        KNNG_TRY(launch(m, p));
         if (dbg_clk) {
             unsigned long long h[8];
             cudaMemcpyAsync(h, dbg_clk, sizeof(h), cudaMemcpyDeviceToHost, st);
@@ -907,6 +931,10 @@ knng_gpu_status knn_u8_sets_impl(const U8Sets& z, uint64_t d, uint64_t k, int me
     if (q_count == 0) return KNNG_GPU_OK;
     if (z.n_b < k + (z.exclude_self ? 1 : 0))
         return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: fewer base rows than k");
+    // TMA sources and the 16-byte copies of the base key offsets.
+    if ((reinterpret_cast<uintptr_t>(z.q_packed) | reinterpret_cast<uintptr_t>(z.b_packed) |
+         reinterpret_cast<uintptr_t>(z.b_norms)) & 15)
+        return fail(KNNG_GPU_INVALID_ARGUMENT, "knng::gpu: packed rows and base key offsets must be 16-byte aligned");
     const ScratchU8 sc = carve_scratch_u8(scratch, q_count, k, scratch_bytes);
     KNNG_CUDA(cudaMemsetAsync(sc.counters, 0, 8, st));
     uint32_t launches = 0;

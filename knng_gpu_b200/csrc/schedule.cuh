@@ -191,6 +191,8 @@ __global__ void merge_partials(const MergeParams p)
     RegTopK<KCAP> tk;
     tk.init(p.k);
     for (uint32_t uu = u_first; uu <= u_last; ++uu) {
+        // Units with an empty range (fewer tail items than units) wrote nothing.
+        if (range_begin(total, s.n_units, uu) == range_begin(total, s.n_units, uu + 1)) continue;
         // The piece of unit uu in this tile is its range's first piece
         // (slot 0) unless the range began in the previous tile (slot 1).
         const uint32_t slot = range_begin(total, s.n_units, uu) < qlo ? 1u : 0u;

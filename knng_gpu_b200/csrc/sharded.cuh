@@ -14,8 +14,9 @@
 //     1M x 128), every rank searches its compute_shard query rows against it,
 //     and the graph rows go to rank 0 by NCCL send/recv (NCCL has no Gatherv).
 //     Non-integer data all-gathers the fp32 rows instead and takes the fp32
-//     path. No host synchronisation before the search: the pair kernel reads
-//     the reduced flag on the device and returns at once for fp32 data.
+//     path. No host synchronisation before the search: the tensor-core
+//     kernels read the reduced flag on the device and return at once for
+//     fp32 data.
 //   ring mode (the base never replicated): rank r's compute_shard rows are its
 //     queries and its base block; in step s it searches block (r - s) mod P
 //     while NCCL already sends that block to rank r + 1 and receives the next
@@ -102,8 +103,10 @@ ShardedLayout sharded_layout(uint64_t n, uint64_t d, uint64_t k, int world, int 
         L.f32s = take(layout_scratch_f32(nullptr, n, d, ms, k).total);
         L.total = L.u + std::max(u8_end, off);
     } else {
-        L.packed = take(2 * ms * pitch);  // two ring buffers
-        L.norms = take(2 * ms * 4);
+        // Two ring buffers, each starting 256-byte aligned (TMA sources;
+        // the key offsets are read 16 bytes at a time).
+        L.packed = take(2 * align_up(ms * pitch, 256));
+        L.norms = take(2 * align_up(ms * 4, 256));
         L.qpacked = take(ms * pitch);
         L.qnorms = take(ms * 4);
         L.tmp_ids = take(ms * k * 4);
@@ -245,8 +248,9 @@ knng_gpu_status sharded_ring(KnngComm* c, const float* shard_rows, uint64_t n, u
         return fail(KNNG_GPU_NOT_SUPPORTED, "knng::gpu: ring mode needs at least k + 1 rows per rank");
     int32_t* flag = reinterpret_cast<int32_t*>(ws + L.flag);
     uint8_t* u = ws + L.u;
-    uint8_t* buf[2] = {u + L.packed, u + L.packed + ms * pitch};
-    int32_t* nbuf[2] = {reinterpret_cast<int32_t*>(u + L.norms), reinterpret_cast<int32_t*>(u + L.norms) + ms};
+    const uint64_t buf_bytes = align_up(ms * pitch, 256), nbuf_bytes = align_up(ms * 4, 256);
+    uint8_t* buf[2] = {u + L.packed, u + L.packed + buf_bytes};
+    int32_t* nbuf[2] = {reinterpret_cast<int32_t*>(u + L.norms), reinterpret_cast<int32_t*>(u + L.norms + nbuf_bytes)};
     uint8_t* qpacked = u + L.qpacked;
     int32_t* qnorms = reinterpret_cast<int32_t*>(u + L.qnorms);
     uint32_t* tmp_ids = reinterpret_cast<uint32_t*>(u + L.tmp_ids);
@@ -265,6 +269,7 @@ knng_gpu_status sharded_ring(KnngComm* c, const float* shard_rows, uint64_t n, u
     KNNG_CUDA(cudaMemcpyAsync(buf[0], qpacked, sh.count * pitch, cudaMemcpyDeviceToDevice, st));
     KNNG_CUDA(cudaMemcpyAsync(nbuf[0], qnorms, sh.count * 4, cudaMemcpyDeviceToDevice, st));
     pm.mark(1);
+    pm.mark(2);  // no separate base exchange: the ring passes blocks during the search
     if (stats) {
         std::memset(stats, 0, sizeof(*stats));
         stats->kernel_launches = 2;
@@ -314,8 +319,7 @@ knng_gpu_status sharded_ring(KnngComm* c, const float* shard_rows, uint64_t n, u
         }
         if (step + 1 < P) KNNG_CUDA(cudaStreamWaitEvent(st, c->ev_comm[cur], 0));
     }
-    pm.mark(2);
-    pm.mark(3);
+    pm.mark(3);  // search, overlapped with the ring exchange
     pm.mark(4);
     uint32_t* my_ids = best_ids[cur_best];
     float* my_d = best_d[cur_best];

@@ -67,7 +67,10 @@ def test_single_process_multi_gpu_equals_oracle(cuda_ok, ring):
     g = torch.cuda.device_count()
     if g < 2:
         pytest.skip("needs 2 GPUs")
-    for kind, n, d, k, metric in [(syn.KIND_UNIFORM_INT, 6007, 128, 10, 0), (syn.KIND_SPARSE_INT, 3001, 784, 64, 1)]:
+    # Shard sizes whose packed blocks and key offsets end off a 16-byte
+    # boundary (3001, 20011 on two ranks) as well as even ones.
+    for kind, n, d, k, metric in [(syn.KIND_UNIFORM_INT, 6007, 128, 10, 0), (syn.KIND_UNIFORM_INT, 3001, 128, 10, 0),
+                                  (syn.KIND_UNIFORM_INT, 20011, 128, 10, 0), (syn.KIND_SPARSE_INT, 3001, 784, 64, 1)]:
         x = syn.generate(kind, 41, n, d, p_zero=0.6)
         out = kg.brute_force_knn_multi(x, k, metric, num_gpus=g, ring=ring)
         oi, od = oracle_knn(x, k, metric)

@@ -77,6 +77,10 @@ def test_u8_cross_set_against_oracle(cuda_ok, metric):
     oi, od = oracle_knn_sets(q, 20_000, b, 7, k, metric, False)
     assert np.array_equal(ids.cpu().numpy().view(np.uint32), oi)
     assert np.array_equal(dists.cpu().numpy(), od)
+    # Base key offsets that are not 16-byte aligned are refused, not misread.
+    with pytest.raises(api.InvalidArgument):
+        api.knn_u8_sets(pk["q"][0], pk["q"][1], 20_000, pk["b"][0][1:], pk["b"][1][1:], 8, d, k, metric, False, ids,
+                        dists, scratch)
 
 
 def test_gpu_recall_matches_reference(cuda_ok):
