@@ -201,10 +201,9 @@ knng_gpu_status knng_gpu_knn_f32(const float* d_x, uint64_t n, uint64_t d, uint6
  * the process exits). Limits and caveats:
  *   - q_count must be <= KNNG_GPU_NOALLOC_MAX_QUERIES, else
  *     KNNG_GPU_INVALID_ARGUMENT;
- *   - the first call in a CUDA context looks up the array's address in that
- *     context (cudaGetSymbolAddress, with the context current) and caches it
- *     per context; knng_gpu_release_cached_buffers empties that cache (call
- *     it after cudaDeviceReset);
+ *   - every call looks up the array's address in the CUDA context current
+ *     on the calling thread (cudaGetSymbolAddress): a host may use its own,
+ *     non-primary context, or reset the device, between calls;
  *   - all calls share the one array: calls that overlap on the GPU (other
  *     streams, other host threads) race and must be serialised by the caller.
  * The call allocates nothing: no cudaMalloc/cudaFree and no allocating

@@ -104,8 +104,6 @@ struct KnnTcParams {
     uint32_t* part_ids;
     uint32_t part_units;         // units whose partial lists fit (0: whole query tiles only)
     const int* skip_flag;        // u8: non-zero -> the data is not integer-valued, do nothing
-    const int32_t* seed_in;      // u8: per query row, an upper bound on its k-th key
-    int32_t* seed_out;           // u8 seeding pass: each query row's k-th key instead of its graph row
     uint32_t debug_flags;        // profiling only: 1 skip filtering, 2 skip insertion, 4 skip TMEM loads
     unsigned long long* debug_clocks;  // profiling only: per-role wait cycles (flag 512)
 };
@@ -639,17 +637,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
             }
             TopK tk;
             tk.init(p.k);
-            // u8: a seeded upper bound on the row's k-th key (from a pass
-            // over a subset of the base) admits only keys <= seed from the
-            // start, so the list sees fewer insertions.
-            int32_t seed_thr = INT_MAX;
-            if constexpr (!Elem::kFloat) {
-                if (p.seed_in && qvalid) {
-                    const int32_t sd = p.seed_in[qlocal];
-                    seed_thr = sd < INT_MAX ? sd + 1 : INT_MAX;
-                }
-            }
-            int32_t thr = min(tk.thr(), seed_thr);
+            int32_t thr = tk.thr();
             // u8: a column can enter the list only if its accumulator exceeds
             // lim (keys are keyoff - 2 acc >= keyoff_min(tile) - 2 acc for L2,
             // -acc for IP); recomputed per tile and after every insertion.
@@ -721,7 +709,7 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                             const uint32_t id = col0 + i;
                             if (key < thr && id != self_id) {
                                 tk.insert_increasing(key, id);
-                                thr = min(tk.thr(), seed_thr);
+                                thr = tk.thr();
                             }
                         }
                     }
@@ -874,8 +862,6 @@ __global__ void __launch_bounds__(64 + 128 * MT * SPLIT, 1)
                     p.part_keys[o + jj] = key;
                     p.part_ids[o + jj] = id;
                 });
-            } else if (p.seed_out) {
-                p.seed_out[qlocal] = tk.thr();
             } else {
                 float* odist = p.out_dists + static_cast<uint64_t>(qlocal) * p.k;
                 bool inexact = false;

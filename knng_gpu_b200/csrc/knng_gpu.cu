@@ -375,7 +375,6 @@ knng_gpu_status launch_tc_t(const TcMaps& m, KnnTcParams p, cudaStream_t st)
             mp.fallback_rows = p.fallback_rows;
             mp.fallback_count = p.fallback_count;
             mp.skip_flag = p.skip_flag;
-            mp.seed_out = p.seed_out;
             merge_partials<METRIC, TopK::kCap><<<units - 1, MT * kTileRows, 0, st>>>(mp);
             KNNG_CUDA(cudaGetLastError());
         }
@@ -612,35 +611,12 @@ knng_gpu_status launch_u8_sets(const U8Sets& z, uint64_t d, uint64_t k, int metr
             cudaMemsetAsync(dbg_clk, 0, 8 * sizeof(unsigned long long), st);
             p.debug_clocks = dbg_clk;
         }
-        auto launch = [&](const TcMaps& mm, const KnnTcParams& pp) {
-            if (mt == 2)
-                return metric == 0 ? launch_u8_k<2, 0>(mm, pp, st, split) : launch_u8_k<2, 1>(mm, pp, st, split);
-            return metric == 0 ? launch_u8_k<1, 0>(mm, pp, st, split) : launch_u8_k<1, 1>(mm, pp, st, split);
-        };
-        // Seeding pass: the queries against the first kSeedRows base rows
-        // give each query an exact upper bound on its k-th key over the whole
-        // base (its k-th key over a subset of the rows); the main pass admits
-        // only keys at or below it. The result is unchanged.
-        bool seeded = z.n_b >= kSeedMinBase && k + 1 <= kSeedRows && k <= 64 && sc.part_units > 0;
-        if (const char* sv = experiment_knob("KNNG_GPU_SEED")) seeded = seeded && std::atoi(sv) != 0;
-        if (seeded) {
-            TcMaps ms = m;
-            KNNG_TRY(make_map(&ms.b0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.b_packed, kSeedRows, data_bytes, pitch));
-            if (metric == 0)
-                KNNG_TRY(make_map(&ms.b1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, z.b_packed + data_bytes, kSeedRows,
-                                  kAugBytes, pitch, kAugBytes));
-            else
-                ms.b1 = ms.b0;
-            KnnTcParams ps = p;
-            ps.n_base = kSeedRows;
-            ps.seed_out = sc.seeds;
-            ps.debug_flags = 0;
-            ps.debug_clocks = nullptr;
-            KNNG_TRY(launch(ms, ps));
-            *launches += 2;
-            p.seed_in = sc.seeds;
-        }
-        KNNG_TRY(launch(m, p));
+        knng_gpu_status s;
+        if (mt == 2)
+            s = metric == 0 ? launch_u8_k<2, 0>(m, p, st, split) : launch_u8_k<2, 1>(m, p, st, split);
+        else
+            s = metric == 0 ? launch_u8_k<1, 0>(m, p, st, split) : launch_u8_k<1, 1>(m, p, st, split);
+        KNNG_TRY(s);
         if (dbg_clk) {
             unsigned long long h[8];
             cudaMemcpyAsync(h, dbg_clk, sizeof(h), cudaMemcpyDeviceToHost, st);
@@ -1452,69 +1428,14 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes]
 
 namespace {
 // The address of a __device__ array belongs to a CUDA context, not to a
-// device number: a host may make a non-primary context current. The cache
-// is therefore keyed by the current context (driver entry point
-// cuCtxGetCurrent) and emptied by knng_gpu_release_cached_buffers.
-using CtxGetCurrentFn = CUresult (*)(CUcontext*);
-constexpr int kNoAllocSlots = 64;
-std::mutex g_noalloc_mutex;
-CUcontext g_noalloc_ctx[kNoAllocSlots] = {};
-void* g_noalloc_ptr[kNoAllocSlots] = {};
-
-knng_gpu_status current_context(CUcontext* out)
-{
-    static CtxGetCurrentFn fn = nullptr;
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        cudaError_t e = cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q);
-        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p)
-            return fail(KNNG_GPU_CUDA_ERROR, "knng::gpu: cuCtxGetCurrent entry point not available");
-        fn = reinterpret_cast<CtxGetCurrentFn>(p);
-    }
-    if (fn(out) != CUDA_SUCCESS) return fail(KNNG_GPU_CUDA_ERROR, "knng::gpu: cuCtxGetCurrent failed");
-    return KNNG_GPU_OK;
-}
-
+// device number, and a host may make a non-primary context current (or
+// destroy one and get a new context with a recycled handle). So the address
+// is resolved on every call, in whatever context is current; once the module
+// is loaded in that context this is a table lookup and allocates nothing.
 knng_gpu_status noalloc_scratch_ptr(void** out)
 {
-    int dev = 0;
-    KNNG_CUDA(cudaGetDevice(&dev));
-    CUcontext ctx = nullptr;
-    KNNG_TRY(current_context(&ctx));
-    if (!ctx) {
-        // No context current yet: the runtime call makes the device's
-        // primary context current.
-        void* probe = nullptr;
-        KNNG_CUDA(cudaGetSymbolAddress(&probe, g_noalloc_scratch));
-        KNNG_TRY(current_context(&ctx));
-    }
-    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    for (int i = 0; i < kNoAllocSlots; ++i)
-        if (g_noalloc_ctx[i] == ctx && g_noalloc_ptr[i]) {
-            *out = g_noalloc_ptr[i];
-            return KNNG_GPU_OK;
-        }
-    void* ptr = nullptr;
-    // With this context current, the symbol resolves to its copy of the array.
-    KNNG_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
-    for (int i = 0; i < kNoAllocSlots; ++i)
-        if (!g_noalloc_ptr[i]) {
-            g_noalloc_ctx[i] = ctx;
-            g_noalloc_ptr[i] = ptr;
-            break;
-        }
-    *out = ptr;
+    KNNG_CUDA(cudaGetSymbolAddress(out, g_noalloc_scratch));
     return KNNG_GPU_OK;
-}
-
-void noalloc_forget_all()
-{
-    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    for (int i = 0; i < kNoAllocSlots; ++i) {
-        g_noalloc_ctx[i] = nullptr;
-        g_noalloc_ptr[i] = nullptr;
-    }
 }
 }  // namespace
 
@@ -1707,7 +1628,6 @@ void knng_gpu_release_cached_buffers(void)
     }
     if (have_cur) cudaSetDevice(cur);
     cudaGetLastError();
-    noalloc_forget_all();
 }
 
 knng_gpu_status knng_gpu_knn_u8_noalloc(const uint8_t* d_packed, const int32_t* d_norms, uint64_t n, uint64_t d,

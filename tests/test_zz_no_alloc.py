@@ -79,3 +79,85 @@ def test_noalloc_matches_regular_entry_twice(cuda_ok, metric, k, n, d, seed):
         assert torch.equal(ids, ref_ids)
         assert torch.equal(dists.view(torch.int32), ref_d.view(torch.int32))
         assert stats.fallback_rows == ref_stats["fallback_rows"]
+
+
+def _driver():
+    lib = ctypes.CDLL("libcuda.so.1")
+    c = ctypes
+    for name, args in [("cuInit", [c.c_uint]), ("cuDeviceGet", [c.c_void_p, c.c_int]),
+                       ("cuCtxCreate_v2", [c.c_void_p, c.c_uint, c.c_int]), ("cuCtxDestroy_v2", [c.c_void_p]),
+                       ("cuCtxPushCurrent_v2", [c.c_void_p]), ("cuCtxPopCurrent_v2", [c.c_void_p]),
+                       ("cuCtxSynchronize", []), ("cuMemAlloc_v2", [c.c_void_p, c.c_size_t]),
+                       ("cuMemFree_v2", [c.c_uint64]), ("cuMemcpyHtoD_v2", [c.c_uint64, c.c_void_p, c.c_size_t]),
+                       ("cuMemcpyDtoH_v2", [c.c_void_p, c.c_uint64, c.c_size_t])]:
+        f = getattr(lib, name)
+        f.argtypes = args
+        f.restype = c.c_int
+    return lib
+
+
+@pytest.mark.gpu
+def test_noalloc_in_a_second_context_then_the_primary_again(cuda_ok):
+    """A host that makes its own (non-primary) context current: the array's
+    address is resolved in that context, and afterwards in the primary one
+    again. Every buffer of the second context is allocated in it through the
+    driver API."""
+    import torch
+
+    n, d, k, metric = 2000, 128, 10, 0
+    x = syn.generate(syn.KIND_UNIFORM_INT, 11, n, d)
+    dev = torch.device("cuda", 0)
+    pitch = api.padded_dim(d)
+    packed = torch.empty((n, pitch), dtype=torch.uint8, device=dev)
+    norms = torch.empty(n, dtype=torch.int32, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    api.pack_u8(torch.from_numpy(x).to(dev), packed, norms, flag)
+    ref_ids = torch.empty((n, k), dtype=torch.int32, device=dev)
+    ref_d = torch.empty((n, k), dtype=torch.float32, device=dev)
+    scratch = torch.empty(api.knn_scratch_bytes(n, k), dtype=torch.uint8, device=dev)
+    api.knn_u8(packed, norms, n, d, 0, n, k, metric, ref_ids, ref_d, scratch)
+    torch.cuda.synchronize()
+    h_packed = packed.cpu().numpy()
+    h_norms = norms.cpu().numpy()
+
+    cu = _driver()
+    assert cu.cuInit(0) == 0
+    cudev = ctypes.c_int()
+    assert cu.cuDeviceGet(ctypes.byref(cudev), torch.cuda.current_device()) == 0
+    ctx = ctypes.c_void_p()
+    assert cu.cuCtxCreate_v2(ctypes.byref(ctx), 0, cudev.value) == 0  # now current
+    bufs = []
+    try:
+        def alloc(nbytes):
+            p = ctypes.c_uint64()
+            assert cu.cuMemAlloc_v2(ctypes.byref(p), nbytes) == 0
+            bufs.append(p.value)
+            return p.value
+
+        d_packed, d_norms = alloc(h_packed.nbytes), alloc(h_norms.nbytes)
+        d_ids, d_dists = alloc(n * k * 4), alloc(n * k * 4)
+        assert cu.cuMemcpyHtoD_v2(d_packed, h_packed.ctypes.data, h_packed.nbytes) == 0
+        assert cu.cuMemcpyHtoD_v2(d_norms, h_norms.ctypes.data, h_norms.nbytes) == 0
+        st = _native.gpu_lib().knng_gpu_knn_u8_noalloc(d_packed, d_norms, n, d, 0, n, k, metric, d_ids, d_dists,
+                                                         None, None)
+        api.check(st)
+        assert cu.cuCtxSynchronize() == 0
+        ids = np.empty((n, k), np.int32)
+        dists = np.empty((n, k), np.float32)
+        assert cu.cuMemcpyDtoH_v2(ids.ctypes.data, d_ids, ids.nbytes) == 0
+        assert cu.cuMemcpyDtoH_v2(dists.ctypes.data, d_dists, dists.nbytes) == 0
+    finally:
+        for p in bufs:
+            cu.cuMemFree_v2(p)
+        popped = ctypes.c_void_p()
+        cu.cuCtxPopCurrent_v2(ctypes.byref(popped))
+        cu.cuCtxDestroy_v2(ctx)
+    assert np.array_equal(ids, ref_ids.cpu().numpy())
+    assert np.array_equal(dists.view(np.int32), ref_d.cpu().numpy().view(np.int32))
+
+    # The primary context again (torch's): same results.
+    ids2 = torch.full((n, k), -1, dtype=torch.int32, device=dev)
+    dists2 = torch.full((n, k), -1.0, dtype=torch.float32, device=dev)
+    _noalloc(packed, norms, n, d, 0, n, k, metric, ids2, dists2, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert torch.equal(ids2, ref_ids) and torch.equal(dists2.view(torch.int32), ref_d.view(torch.int32))
