@@ -48,6 +48,9 @@ PARITY_SEED = 0x5EED
 # Query rows per reference-arm step, sized so that a step takes a few seconds
 # on 16 host cores (the canonical loop runs at ~1 ns per coordinate per core).
 REF_QUERIES = {1: 10_000, 2: 2048, 3: 512, 4: 64, 5: 16}
+# Seeded query rows of the one-GPU parity check, which also times the CPU
+# baseline: ~10-30 s of reference work on 16 host cores (all of config 1).
+CPU_SAMPLE = {1: 10_000, 2: 8192, 3: 2048, 4: 256, 5: 256}
 
 
 def parse():
@@ -347,7 +350,8 @@ def main() -> None:
         else:
             g_ids, g_d = out
             x_full = syn.generate_config(cfg, n)
-            q = syn.sample_ids(cfg.seed ^ PARITY_SEED, n, min(args.parity_rows, n))
+            rows = max(args.parity_rows, CPU_SAMPLE.get(args.config, 0)) if world == 1 else args.parity_rows
+            q = syn.sample_ids(cfg.seed ^ PARITY_SEED, n, min(rows, n))
             threads = os.cpu_count() or 1
             r_ids, r_d, secs = ref_subset(lib, x_full, k, cfg.metric, q, threads)
             qi = torch.from_numpy(q.astype(np.int64)).to(g_ids.device)
