@@ -75,7 +75,11 @@ int knng_gpu_device_count(void);
  * `ids`/`dists` are caller-allocated n*k arrays (Knng::neighbors/distances).
  * Runs on the current CUDA device. Device buffers are cached per device and
  * reused by later calls (see knng_gpu_release_cached_buffers); calls on one
- * device are serialised. `stats` may be NULL. */
+ * device are serialised. `stats` may be NULL. Host buffers may be pageable or
+ * pinned: pinned ones (cudaMallocHost / cudaHostRegister) are copied
+ * directly; pageable ones of 4 MiB or more go through a ring of four 32 MiB
+ * pinned chunks that the library allocates on first use and keeps per
+ * device, with the host-side copies spread over up to 8 threads. */
 knng_gpu_status knng_gpu_brute_force(const float* data, uint64_t n, uint64_t d, uint64_t k, int metric,
                                      uint32_t* ids, float* dists, knng_gpu_stats* stats);
 
@@ -88,9 +92,10 @@ knng_gpu_status knng_gpu_brute_force(const float* data, uint64_t n, uint64_t d, 
 knng_gpu_status knng_gpu_brute_force_u8(const uint8_t* rows, uint64_t n, uint64_t d, uint64_t row_stride, uint64_t k,
                                         int metric, uint32_t* ids, float* dists, knng_gpu_stats* stats);
 
-/* Free the device buffers and stream that knng_gpu_brute_force keeps per
- * device between calls (they are grown on demand and otherwise held until
- * process exit). No counterpart in the reference. */
+/* Free the device buffers, pinned staging chunks and stream that
+ * knng_gpu_brute_force keeps per device between calls (they are grown on
+ * demand and otherwise held until process exit). No counterpart in the
+ * reference. */
 void knng_gpu_release_cached_buffers(void);
 
 /* ---- device-resident API (inputs already in HBM) ------------------------

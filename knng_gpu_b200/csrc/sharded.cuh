@@ -376,6 +376,7 @@ struct MultiDevice {
     cudaStream_t stream = nullptr;
     void *ws = nullptr, *slice = nullptr, *ids = nullptr, *dists = nullptr;
     uint64_t ws_cap = 0, slice_cap = 0, ids_cap = 0, dists_cap = 0;
+    HostStage stage;  // pinned chunks for host buffers the caller did not pin
 };
 struct MultiCache {
     std::mutex mutex;
@@ -389,6 +390,7 @@ void multi_release_locked()
     for (size_t g = 0; g < g_multi.dev.size(); ++g) {
         MultiDevice& m = g_multi.dev[g];
         cudaSetDevice(static_cast<int>(g));
+        stage_release(m.stage);
         cudaFree(m.ws);
         cudaFree(m.slice);
         cudaFree(m.ids);
@@ -550,13 +552,13 @@ knng_gpu_status knng_gpu_brute_force_multi(const float* data, uint64_t n, uint64
                 KNNG_TRY(grow(&m.ids, &m.ids_cap, n * k * 4));
                 KNNG_TRY(grow(&m.dists, &m.dists_cap, n * k * 4));
             }
-            if (cnt) KNNG_CUDA(cudaMemcpyAsync(m.slice, data + lo * d, cnt * d * 4, cudaMemcpyHostToDevice, m.stream));
+            KNNG_TRY(copy_to_device(m.stage, m.slice, data + lo * d, cnt * d * 4, m.stream));
             KNNG_TRY(knng_gpu_brute_force_sharded(static_cast<const float*>(m.slice), n, d, k, metric, mode, m.comm,
                                                   static_cast<uint32_t*>(m.ids), static_cast<float*>(m.dists), m.ws,
                                                   m.ws_cap, m.stream, stats ? &st[g] : nullptr));
             if (g == 0) {
-                KNNG_CUDA(cudaMemcpyAsync(ids, m.ids, n * k * 4, cudaMemcpyDeviceToHost, m.stream));
-                KNNG_CUDA(cudaMemcpyAsync(dists, m.dists, n * k * 4, cudaMemcpyDeviceToHost, m.stream));
+                KNNG_TRY(copy_to_host(m.stage, ids, m.ids, n * k * 4, m.stream));
+                KNNG_TRY(copy_to_host(m.stage, dists, m.dists, n * k * 4, m.stream));
             }
             KNNG_CUDA(cudaStreamSynchronize(m.stream));
             return KNNG_GPU_OK;

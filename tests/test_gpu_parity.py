@@ -123,6 +123,34 @@ def test_device_api_and_determinism(cuda_ok):
     assert s1["knn_ms"] > 0
 
 
+def test_host_api_staged_copies_match_device_api(cuda_ok):
+    """Host buffers the caller did not pin travel through the library's ring
+    of pinned chunks (input of 5 chunks, so the ring wraps; both outputs above
+    the staging threshold). The graph equals the device-resident build bit for
+    bit, for fp32 rows and for strided byte rows."""
+    import torch
+
+    n, d, k = 600_000, 64, 8
+    rng = np.random.default_rng(23)
+    vals = rng.integers(0, 256, size=(n, d), dtype=np.uint8)
+    x = vals.astype(np.float32)
+    g = kg.brute_force_knn(x, k)
+    di, dd, _ = kg.brute_force_knn_device(torch.from_numpy(x).cuda(), k)
+    di = di.cpu().numpy().view(np.uint32)
+    dd = dd.cpu().numpy()
+    assert np.array_equal(g.neighbors.reshape(n, k), di)
+    assert np.array_equal(g.distances.reshape(n, k).view(np.uint32), dd.view(np.uint32))
+    buf = np.empty((n, d + 4), dtype=np.uint8)
+    buf[:, :d] = vals
+    buf[:, d:] = 7
+    gb = kg.brute_force_knn_u8(buf, k, d=d)
+    assert np.array_equal(gb.neighbors.reshape(n, k), di)
+    q = syn.sample_ids(5, n, 16)
+    oi, od = oracle_knn(x, k, 0, queries=q)
+    assert np.array_equal(di[q.astype(np.int64)], oi)
+    assert np.array_equal(dd[q.astype(np.int64)].view(np.uint32), od.view(np.uint32))
+
+
 def test_config3_subset_against_oracle(cuda_ok):
     """Full 1M x 128 build; 64 seeded query rows checked against the oracle,
     every row checked for the size-independent properties."""
