@@ -67,7 +67,7 @@ struct PairParams {
     uint32_t* fallback_count;
     int* error;
     const int* skip_flag;  // optional: non-zero -> the data is not integer-valued, do nothing
-    const int32_t* seed_in;  // optional: per query row, an upper bound on its k-th key
+    const int32_t* seed_in;  // optional: per query row, an upper bound on the keys its list admits
     int32_t* seed_out;       // seeding pass: write each query row's k-th key instead of its list
     long long wait_limit;  // clock cycles before a wait gives up
     uint32_t test_mode;    // 1: the leader's producer withholds one arrival (timeout test)
@@ -591,13 +591,14 @@ __global__ void __launch_bounds__(pair_threads(EPI), 1) knn_pair_kernel(const __
             // Segment done (slice 0): final graph rows, or a partial list of a
             // query tile cut between pairs; in the seeding pass only the k-th key.
             if (qvalid && slice == 0) {
+                const int32_t bound = seed_thr == INT_MAX ? INT_MAX : seed_thr - 1;
                 if (complete && p.seed_out) {
-                    p.seed_out[qlocal] = tk.thr();
+                    p.seed_out[qlocal] = min(tk.thr(), bound);
                 } else if (complete) {
                     const int32_t qnorm =
                         kL2 ? packed_sq_norm(p.query_packed, p.pitch, p.data_bytes, p.query_norms, qlocal) : 0;
                     emit_graph_row<METRIC>(tk, p.k, qlocal, qnorm, p.out_ids, p.out_dists, p.fallback_rows,
-                                           p.fallback_count);
+                                           p.fallback_count, bound);
                 } else {
                     const uint64_t o = (static_cast<uint64_t>(pslot) * kPairTile + cta * kTileRows + row) * p.k;
                     tk.for_each(p.k, [&](int jj, int32_t key, uint32_t id) {

@@ -520,6 +520,11 @@ struct U8Sets {
     uint64_t n_b;
     uint64_t b_id0;
     int exclude_self;
+    // Optional, per query row: an exact upper bound on the keys worth
+    // keeping (the running k-th key of a ring build). The pair kernel then
+    // admits only keys at or below it, and its lists may hold fewer than k
+    // entries; the single-CTA kernel ignores it (full lists are still right).
+    const int32_t* seed = nullptr;
 };
 
 // Query tiles per CTA of the fused u8 kernel: two need k <= 32 (register
@@ -722,6 +727,7 @@ knng_gpu_status launch_pair_t(const PairMaps& m, PairParams& pp, uint32_t max_pa
         mp.out_ids = pp.out_ids;
         mp.out_dists = pp.out_dists;
         mp.seed_out = pp.seed_out;
+        mp.seed_in = pp.seed_in;
         mp.query_norms = pp.query_norms;
         mp.query_packed = pp.query_packed;
         mp.pitch = pp.pitch;
@@ -847,11 +853,14 @@ knng_gpu_status launch_u8_pair(const U8Sets& z, uint64_t d, uint64_t k, int metr
         PairParams ps = pp;
         ps.n_base = kSeedRows;
         ps.sched.n_btiles = static_cast<uint32_t>(kSeedRows / kPairTile);
+        ps.seed_in = z.seed;  // an outside bound caps the seeded one
         ps.seed_out = sc.seeds;
         ps.debug_flags = 0;
         KNNG_TRY(metric == 0 ? launch_pair_k<0>(ms, ps, sc.part_units, st, launches, nullptr)
                              : launch_pair_k<1>(ms, ps, sc.part_units, st, launches, nullptr));
         pp.seed_in = sc.seeds;
+    } else {
+        pp.seed_in = z.seed;
     }
     KNNG_TRY(metric == 0 ? launch_pair_k<0>(m, pp, sc.part_units, st, launches, nullptr)
                          : launch_pair_k<1>(m, pp, sc.part_units, st, launches, nullptr));

@@ -103,6 +103,7 @@ struct MergeParams {
     uint32_t* out_ids;           // n_queries x k graph rows
     float* out_dists;
     int32_t* seed_out;           // seeding pass: the k-th key per query instead
+    const int32_t* seed_in;      // optional: per query an upper bound on the keys its list admits
     const int32_t* query_norms;  // key offset per query row (L2)
     const uint8_t* query_packed; // packed query rows (augmentation bytes give |q|^2)
     uint32_t pitch;
@@ -134,25 +135,31 @@ __device__ __forceinline__ int32_t packed_sq_norm(const uint8_t* packed, uint32_
 // Graph row of query qlocal from its sorted (key, id) list: distances
 // |q|^2 + key (L2) or key (inner product) as fp32; rows whose fp32 sums may
 // round (L2: k-th distance >= 2^24; inner product: largest dot >= 2^24) are
-// appended to the fallback list for the exact kernel.
+// appended to the fallback list for the exact kernel. `bound` is the largest
+// key the list could admit (INT_MAX: none). A list searched under an outside
+// bound (the running k-th key of a ring build) may hold fewer than k
+// entries; its empty slots are emitted as (id 0xFFFFFFFF, +inf), which sort
+// after every real entry when the lists are merged, and its exactness test
+// uses the bound in place of the missing k-th key.
 template <int METRIC, class TopK>
 __device__ inline void emit_graph_row(TopK& tk, uint32_t k, uint32_t qlocal, int32_t qnorm, uint32_t* out_ids,
-                                      float* out_dists, uint32_t* fallback_rows, uint32_t* fallback_count)
+                                      float* out_dists, uint32_t* fallback_rows, uint32_t* fallback_count,
+                                      int32_t bound = INT_MAX)
 {
     uint32_t* oid = out_ids + static_cast<uint64_t>(qlocal) * k;
     float* odist = out_dists + static_cast<uint64_t>(qlocal) * k;
     bool inexact;
     if constexpr (METRIC == 0) {
-        inexact = static_cast<int64_t>(qnorm) + tk.thr() >= (1 << 24);
+        inexact = static_cast<int64_t>(qnorm) + min(tk.thr(), bound) >= (1 << 24);
         tk.for_each(k, [&](int jj, int32_t key, uint32_t id) {
             oid[jj] = id;
-            odist[jj] = __int2float_rn(qnorm + key);
+            odist[jj] = key == INT_MAX ? __int_as_float(0x7F800000) : __int2float_rn(qnorm + key);
         });
     } else {
         inexact = -static_cast<int64_t>(tk.best(k)) >= (1 << 24);
         tk.for_each(k, [&](int jj, int32_t key, uint32_t id) {
             oid[jj] = id;
-            odist[jj] = -__int2float_rn(-key);
+            odist[jj] = key == INT_MAX ? __int_as_float(0x7F800000) : -__int2float_rn(-key);
         });
     }
     if (inexact) {
@@ -203,13 +210,15 @@ __global__ void merge_partials(const MergeParams p)
             if (key_gt(tk.thr(), tk.thr_id(), key, id)) tk.insert(key, id);
         }
     }
+    const int32_t bound = p.seed_in ? p.seed_in[qlocal] : INT_MAX;
     if (p.seed_out) {
-        p.seed_out[qlocal] = tk.thr();
+        p.seed_out[qlocal] = min(tk.thr(), bound);
         return;
     }
     const int32_t qnorm =
         METRIC == 0 ? packed_sq_norm(p.query_packed, p.pitch, p.data_bytes, p.query_norms, qlocal) : 0;
-    emit_graph_row<METRIC>(tk, p.k, qlocal, qnorm, p.out_ids, p.out_dists, p.fallback_rows, p.fallback_count);
+    emit_graph_row<METRIC>(tk, p.k, qlocal, qnorm, p.out_ids, p.out_dists, p.fallback_rows, p.fallback_count,
+                           bound);
 }
 
 }  // namespace knng_b200

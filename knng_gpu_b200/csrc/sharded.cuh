@@ -71,7 +71,7 @@ uint64_t replicate_slice_rows(uint64_t n, int world)
 struct ShardedLayout {
     uint64_t flag, out_ids, out_dists, u;        // common part
     uint64_t packed, norms, scratch;             // u8 (relative to u)
-    uint64_t qpacked, qnorms, tmp_ids, tmp_d, best_ids, best_d;  // ring extras (relative to u)
+    uint64_t qpacked, qnorms, tmp_ids, tmp_d, best_ids, best_d, bound;  // ring extras (relative to u)
     uint64_t x, f32s;                            // fp32 (relative to u)
     uint64_t total;
 };
@@ -113,6 +113,7 @@ ShardedLayout sharded_layout(uint64_t n, uint64_t d, uint64_t k, int world, int 
         L.tmp_d = take(ms * k * 4);
         L.best_ids = take(ms * k * 4);
         L.best_d = take(ms * k * 4);
+        L.bound = take(ms * 4);
         L.scratch = take(scratch_u8_bytes(ms, k));
         L.total = L.u + off;
     }
@@ -236,6 +237,31 @@ knng_gpu_status sharded_replicate(KnngComm* c, const float* slice, uint64_t n, u
     return KNNG_GPU_OK;
 }
 
+// Per query row of a ring build: an exact upper bound on the keys that can
+// still enter its k best, from the running k-th distance D of the blocks
+// searched so far (L2: D - |q|^2, inner product: D itself). D is exact when
+// |D| < 2^24 (integer data: every partial sum of the reference's fp32 loop is
+// an integer below it); otherwise no bound (INT_MAX).
+template <int METRIC>
+__global__ void ring_bound_kernel(const float* __restrict__ best_d, uint64_t rows, uint32_t k,
+                                  const uint8_t* __restrict__ qpacked, const int32_t* __restrict__ qnorms,
+                                  uint32_t pitch, uint32_t data_bytes, int32_t* __restrict__ bound)
+{
+    const uint64_t r = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    const float dk = best_d[r * k + k - 1];
+    int32_t b = INT_MAX;
+    if (fabsf(dk) < 16777216.0f) {
+        const int32_t di = static_cast<int32_t>(dk);
+        if constexpr (METRIC == 0) {
+            b = di - packed_sq_norm(qpacked, pitch, data_bytes, qnorms, static_cast<uint32_t>(r));
+        } else {
+            b = di;
+        }
+    }
+    bound[r] = b;
+}
+
 knng_gpu_status sharded_ring(KnngComm* c, const float* shard_rows, uint64_t n, uint64_t d, uint64_t k, int metric,
                              uint32_t* ids, float* dists, uint8_t* ws, const ShardedLayout& L, cudaStream_t st,
                              knng_gpu_stats* stats)
@@ -257,6 +283,7 @@ knng_gpu_status sharded_ring(KnngComm* c, const float* shard_rows, uint64_t n, u
     float* tmp_d = reinterpret_cast<float*>(u + L.tmp_d);
     uint32_t* best_ids[2] = {reinterpret_cast<uint32_t*>(u + L.best_ids), reinterpret_cast<uint32_t*>(ws + L.out_ids)};
     float* best_d[2] = {reinterpret_cast<float*>(u + L.best_d), reinterpret_cast<float*>(ws + L.out_dists)};
+    int32_t* bound = reinterpret_cast<int32_t*>(u + L.bound);
     PhaseMarks pm{c, st, stats != nullptr};
     pm.mark(0);
     KNNG_CUDA(cudaMemsetAsync(flag, 0, 4, st));
@@ -295,8 +322,22 @@ knng_gpu_status sharded_ring(KnngComm* c, const float* shard_rows, uint64_t n, u
             KNNG_CUDA(cudaEventRecord(c->ev_comm[cur], c->comm_stream));
         }
         // Global ids; the own block excludes self by id (brute_force_mpi.cpp:80-82).
-        const U8Sets z{qpacked, qnorms, sh.count, sh.start, buf[cur], nbuf[cur], bsh.count, bsh.start,
-                       blk == r ? 1 : 0};
+        U8Sets z{qpacked, qnorms, sh.count, sh.start, buf[cur], nbuf[cur], bsh.count, bsh.start, blk == r ? 1 : 0};
+        if (step > 0) {
+            // From the second block on, only keys at or below the running
+            // k-th key can change a row's list.
+            const uint32_t db = static_cast<uint32_t>(u8_data_bytes(d));
+            const uint32_t grid = static_cast<uint32_t>((sh.count + 255) / 256);
+            if (metric == 0)
+                ring_bound_kernel<0><<<grid, 256, 0, st>>>(best_d[cur_best], sh.count, static_cast<uint32_t>(k),
+                                                           qpacked, qnorms, static_cast<uint32_t>(pitch), db, bound);
+            else
+                ring_bound_kernel<1><<<grid, 256, 0, st>>>(best_d[cur_best], sh.count, static_cast<uint32_t>(k),
+                                                           qpacked, qnorms, static_cast<uint32_t>(pitch), db, bound);
+            KNNG_CUDA(cudaGetLastError());
+            if (stats) ++stats->kernel_launches;
+            z.seed = bound;
+        }
         uint32_t* out_i = step == 0 ? best_ids[0] : tmp_ids;
         float* out_d = step == 0 ? best_d[0] : tmp_d;
         knng_gpu_stats bs{};

@@ -32,7 +32,14 @@ def main():
             print(f"n={n} d={d} k={k} metric={metric} world={dist.get_world_size()} equal={same}", flush=True)
             ok &= same
     # ring pass of base blocks (integer data)
-    for (kind, n, d, k, metric) in [(syn.KIND_SPARSE_INT, 5003, 784, 64, 1), (syn.KIND_UNIFORM_INT, 20011, 128, 10, 0)]:
+    # Blocks on the CTA-pair kernel (d > 256) get the running k-th key of the
+    # blocks before them as an outside bound: small blocks (no seeding pass),
+    # L2 and inner product, and blocks above the seeding threshold (the
+    # seeding pass runs under the outside bound too).
+    for (kind, n, d, k, metric) in [(syn.KIND_SPARSE_INT, 5003, 784, 64, 1), (syn.KIND_UNIFORM_INT, 20011, 128, 10, 0),
+                                     (syn.KIND_UNIFORM_INT, 6007, 300, 16, 0),
+                                     (syn.KIND_SPARSE_INT, 300007, 320, 32, 1),
+                                     (syn.KIND_UNIFORM_INT, 300007, 320, 16, 0)]:
         x = syn.generate(kind, 77, n, d, p_zero=0.6)
         rb = ShardedBuilder(n, d, k, metric, MODE_RING)
         lo, hi = rb.slice_bounds

@@ -24,7 +24,7 @@ def test_two_gpu_sharded_build_equals_single_gpu(cuda_ok):
                         str(HERE / "dist_worker.py")], capture_output=True, text=True, timeout=900, env=env)
     print(r.stdout[-4000:], r.stderr[-4000:])
     assert r.returncode == 0
-    assert r.stdout.count("equal=True") == 5
+    assert r.stdout.count("equal=True") == 8
 
 
 def test_python_cli_two_gpus_equals_oracle(cuda_ok, tmp_path):
@@ -70,7 +70,8 @@ def test_single_process_multi_gpu_equals_oracle(cuda_ok, ring):
     # Shard sizes whose packed blocks and key offsets end off a 16-byte
     # boundary (3001, 20011 on two ranks) as well as even ones.
     for kind, n, d, k, metric in [(syn.KIND_UNIFORM_INT, 6007, 128, 10, 0), (syn.KIND_UNIFORM_INT, 3001, 128, 10, 0),
-                                  (syn.KIND_UNIFORM_INT, 20011, 128, 10, 0), (syn.KIND_SPARSE_INT, 3001, 784, 64, 1)]:
+                                  (syn.KIND_UNIFORM_INT, 20011, 128, 10, 0), (syn.KIND_SPARSE_INT, 3001, 784, 64, 1),
+                                  (syn.KIND_UNIFORM_INT, 4001, 300, 16, 0)]:
         x = syn.generate(kind, 41, n, d, p_zero=0.6)
         out = kg.brute_force_knn_multi(x, k, metric, num_gpus=g, ring=ring)
         oi, od = oracle_knn(x, k, metric)
