@@ -60,7 +60,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=3)
-    ap.add_argument("--n", type=int, default=0, help="override n (smaller runs of the same recipe)")
+    # --rows is the spelling to use under torch.distributed.run, whose own
+    # parser takes a bare --n for an abbreviation of its --nnodes/--nproc-per-node.
+    ap.add_argument("--n", "--rows", dest="n", type=int, default=0,
+                    help="override n (smaller runs of the same recipe)")
     ap.add_argument("--parity-rows", type=int, default=256)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
